@@ -1,0 +1,336 @@
+"""Decode throughput of the B200 megakernel on BASELINE's headline workload.
+
+Workload (the metric's config): Qwen3.5-0.8B hybrid text model, seeded
+random-init bf16 weights, batch 1, a 512-token uniform-random prompt, then greedy decode at
+4096-slot KV capacity with carried conv / recurrent state. One bench "step" = one decode token
+(one launch of the persistent decode kernel).
+
+  value  device-timed tokens/s of the K timed steps, inputs resident in HBM (each step's token
+         is the previous step's fused argmax, read on the device)
+  e2e    the same metric through the public runner path with host buffers: per step a pinned
+         host->device copy of token id + position and a device->host read of the next token,
+         then a host sync (wall clock over the K steps)
+  roofline  algorithmic bytes per token / mean launch time vs the measured HBM copy peak
+  cpu_baseline  the CPU oracle (a port of the reference step) on this host's cores, bounded
+Multi-GPU (torchrun, one process per GPU): independent replicas, no collective on the data
+path; the timed region is bracketed by barriers and the slowest rank's time is reported.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "decode tok/s at batch 1 (Qwen3.5-0.8B, 4K ctx); % of HBM roofline"
+UNIT = "tokens/s"
+WORKLOAD = "qwen3.5-0.8b decode, batch 1, 512-token random prompt, 4096-slot capacity"
+PROFILE = ROOT / "profiles" / "decode_megakernel_qwen3.5-0.8b.md"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", default="qwen3.5-0.8b")
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--capacity", type=int, default=4096)
+    ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def algorithmic_bytes(g, context):
+    """Bytes one decode token must move: every weight once (tied lm_head counted once, embedding
+    row excluded), recurrent + conv state read and written, KV prefix read plus one slot written."""
+    from xinfer_b200 import synthetic
+
+    total = 0
+    for name, (shape, _) in synthetic.parameter_shapes(g).items():
+        if name == "model.embed_tokens.weight":
+            continue
+        n = 1
+        for s in shape:
+            n *= s
+        total += 2 * n
+    total += 2 * g.vocab * g.hidden  # lm_head (tied to the embedding)
+    n_delta = sum(g.is_delta(i) for i in range(g.num_layers))
+    n_attn = g.num_layers - n_delta
+    rec = g.lin_value_heads * g.lin_head_dim * g.lin_head_dim * 4
+    conv = g.conv_channels * g.conv_width * 2
+    total += n_delta * 2 * (rec + conv)
+    kv_token = 2 * g.num_kv_heads * g.head_dim * 2
+    total += n_attn * kv_token * (context + 1)
+    return total
+
+
+def measured_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_from_profile():
+    if not PROFILE.exists():
+        return None
+    for line in PROFILE.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        mhz, max_mhz, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                max_mhz = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not mhz:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        top = sorted(mhz)[len(mhz) // 4:] or mhz  # samples under load
+        return {"sm_mhz": statistics.median(top), "sm_max_mhz": max_mhz, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+def cpu_baseline(args, g, budget_s):
+    """The CPU oracle (port of the reference step) on this host: decode tokens of the same model
+    at a short context until the budget is spent."""
+    from oracle import qwen_step as O
+    from xinfer_b200 import synthetic
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    sd = synthetic.make_state_dict(g, seed=0)
+    W = O.prepare_weights(sd)
+    del sd
+    state = O.allocate_state(g, 64, rows=1)
+    prompt = synthetic.random_prompt(g, 64, seed=0)
+    O.decode_step(g, W, [prompt[0]], [0], state, [1], [1])  # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while n < 63 and (time.perf_counter() - t0 < budget_s or n < 2):
+        _, state = O.decode_step(g, W, [prompt[n + 1]], [n + 1], state, [n + 2], [1])
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{n} decode tokens of the CPU oracle at context 2..{n + 1}, fp32 torch on "
+                      f"{threads} threads"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from xinfer_b200 import configs
+
+    g = configs.get(args.config)
+    res = cpu_baseline(args, g, budget_s=min(120.0, 4.0 * max(1, args.steps) ** 0.5 * 3))
+    line = {
+        "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / res["value"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD + " (CPU sample)", "model": args.config, "global_batch": 1,
+                   "seq_len": args.capacity, "parallelism": "cpu"},
+        "cpu_baseline": res,
+        "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+
+    from xinfer_b200 import configs, synthetic
+    from xinfer_b200.engine import Engine, Runner
+
+    g = configs.get(args.config)
+    weights = synthetic.make_state_dict(g, seed=0, device=dev)
+    eng = Engine(g, weights, capacity=args.capacity, device=dev)
+    runner = Runner(eng)
+    prompt = synthetic.random_prompt(g, args.prompt, seed=1000 + rank)
+    if args.prompt + 2 * (args.warmup + args.steps) > args.capacity:
+        raise SystemExit("prompt + steps exceed the KV capacity")
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    # ---- value: device-resident greedy decode ------------------------------------------------
+    runner.reset()
+    runner.prefill(prompt)
+    start = args.prompt
+    total = args.warmup + args.steps
+    tok = [torch.zeros(1, dtype=torch.int64, device=dev) for _ in range(2)]
+    tok[0].copy_(runner.next_tokens[:1])
+    pos = torch.arange(start, start + total, dtype=torch.int64, device=dev)
+
+    def device_step(k):
+        eng.launch(tok[k % 2], pos[k:k + 1], [start + k + 1], [1], runner.state, runner.state,
+                   runner.logits, tok[(k + 1) % 2])
+
+    for k in range(args.warmup):
+        device_step(k)
+    eng.check_device_error()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clocks:
+        ev0.record(stream)
+        for k in range(args.warmup, total):
+            device_step(k)
+        ev1.record(stream)
+        barrier()
+    ms = ev0.elapsed_time(ev1)
+    eng.check_device_error()
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * args.steps / (ms / 1000.0)
+    mean_launch_s = ms / 1000.0 / args.steps
+
+    # ---- e2e: public runner path with host buffers -------------------------------------------
+    runner.reset()
+    runner.prefill(prompt)
+    host_in = torch.zeros(2, dtype=torch.int64).pin_memory()
+    host_out = torch.zeros(1, dtype=torch.int64).pin_memory()
+    dev_in = torch.zeros(2, dtype=torch.int64, device=dev)
+    next_host = runner.next_token()
+
+    def e2e_step(k, token):
+        host_in[0] = token
+        host_in[1] = start + k
+        dev_in.copy_(host_in, non_blocking=True)
+        eng.launch(dev_in[0:1], dev_in[1:2], [start + k + 1], [1], runner.state, runner.state,
+                   runner.logits, runner.next_tokens)
+        host_out.copy_(runner.next_tokens[:1], non_blocking=True)
+        stream.synchronize()
+        return int(host_out[0])
+
+    for k in range(args.warmup):
+        next_host = e2e_step(k, next_host)
+    barrier()
+    t0 = time.perf_counter()
+    for k in range(args.warmup, total):
+        next_host = e2e_step(k, next_host)
+    e2e_s = time.perf_counter() - t0
+    eng.check_device_error()
+    barrier()
+    if dist is not None:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = world * args.steps / e2e_s
+
+    ctx_mean = start + args.warmup + (args.steps + 1) / 2.0
+    alg = algorithmic_bytes(g, ctx_mean)
+    peak, peak_kind = measured_peak()
+    achieved = alg / mean_launch_s / 1e9
+    traffic = traffic_from_profile()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "model": args.config, "global_batch": world,
+                   "seq_len": args.capacity, "prompt": args.prompt,
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (1.5 GB of weights per step)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": alg, "traffic": traffic},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 8},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args, g, args.cpu_seconds)
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

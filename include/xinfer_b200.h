@@ -1,0 +1,145 @@
+/*
+ * xinfer_b200 — C ABI of the B200 (sm_100a) decode step for the Qwen3 and Qwen3.5 families.
+ *
+ * Plain C: device pointers, sizes and an opaque stream; no torch types. Every entry point
+ * returns 0 on success and a nonzero XB_ERR_* code on failure; xb_last_error() gives the
+ * message of the calling thread's most recent failure.
+ *
+ * The entry points replace the following reference interfaces (paths inside tqxia/xinfer):
+ *   xb_decode_step          compiler/qwen35/model.py:162-183 (ModelStep.forward, T == 1) and
+ *                           compiler/qwen3/model.py:70-95, as run from decode.pt2 by
+ *                           runtime/common/runner.h:30-78 (Runner::step_batch / run_inputs).
+ *                           Also fuses the argmax of runtime/common/generation.h:39.
+ *
+ * Memory layout of every tensor is the reference's (contiguous, row-major):
+ *   KV cache       bf16 [rows, kv_heads, capacity, head_dim]     updated in place
+ *   conv state     bf16 [rows, conv_channels, conv_width]        replaced (read in, write out)
+ *   recurrent      fp32 [rows, value_heads, key_dim, value_dim]  replaced (read in, write out)
+ *   logits         bf16 [B, vocab]
+ */
+#ifndef XINFER_B200_H
+#define XINFER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define XB_ABI_VERSION 1
+
+#define XB_MAX_LAYERS 64
+#define XB_MAX_BATCH 8
+
+enum {
+  XB_OK = 0,
+  XB_ERR_INVALID = 1,   /* bad argument, geometry or size */
+  XB_ERR_CUDA = 2,      /* a CUDA runtime call failed */
+  XB_ERR_DEVICE = 3,    /* the kernel reported a device-side error (bounded wait expired) */
+  XB_ERR_UNSUPPORTED = 4
+};
+
+enum { XB_FAMILY_QWEN3 = 1, XB_FAMILY_QWEN35 = 2 };
+enum { XB_LAYER_ATTENTION = 0, XB_LAYER_DELTANET = 1 };
+
+/* Model geometry. Field meaning follows the HF configs that the reference loads
+ * (compiler/qwen3/model.py:16-26, compiler/qwen35/model.py:21-42). */
+typedef struct XbGeometry {
+  int32_t family;            /* XB_FAMILY_* */
+  int32_t num_layers;
+  int32_t hidden;
+  int32_t intermediate;
+  int32_t vocab;
+  int32_t num_q_heads;       /* full-attention layers */
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t rotary_dim;        /* head_dim for Qwen3; head_dim * partial_rotary_factor for Qwen3.5 */
+  int32_t lin_key_heads;     /* DeltaNet layers (Qwen3.5 only) */
+  int32_t lin_value_heads;
+  int32_t lin_head_dim;      /* key dim == value dim == 128 */
+  int32_t conv_width;        /* 4 */
+  int32_t capacity;          /* KV slots per row */
+  int32_t state_rows;        /* allocated rows of every state tensor (8 in the reference) */
+  float rms_eps;
+  float rope_theta;
+  const float *rope_inv_freq;        /* host, rotary_dim/2 values, or NULL: xb_rope_inv_freq() */
+  int32_t layer_kind[XB_MAX_LAYERS]; /* XB_LAYER_* */
+} XbGeometry;
+
+/* Per-layer device pointers to bf16 weights in the HF layout ([out, in] for linears). */
+typedef struct XbLayerWeights {
+  const void *input_norm, *post_norm;
+  /* full attention */
+  const void *q_proj, *k_proj, *v_proj, *o_proj, *q_norm, *k_norm;
+  /* Gated DeltaNet (the reference's packed in_proj 8224 rows may be passed as four views) */
+  const void *in_qkv, *in_z, *in_b, *in_a, *conv_w, *a_log, *dt_bias, *gnorm, *out_proj;
+  /* SwiGLU MLP */
+  const void *gate, *up, *down;
+} XbLayerWeights;
+
+typedef struct XbModelWeights {
+  const void *embed;       /* [vocab, hidden] */
+  const void *final_norm;  /* [hidden] */
+  const void *lm_head;     /* [vocab, hidden]; == embed when tied */
+  XbLayerWeights layers[XB_MAX_LAYERS];
+} XbModelWeights;
+
+/* Per-layer state pointers for one step. Attention layers use k_cache / v_cache; DeltaNet
+ * layers use conv_in / rec_in (read) and conv_out / rec_out (written). An output either is a
+ * distinct buffer (the reference's "replace" contract: inputs stay unmodified) or equals its
+ * input pointer exactly (update in place); partial overlap is invalid. Pointers address row 0;
+ * rows [0, B) are read and written, rows >= B are never touched. */
+typedef struct XbLayerState {
+  void *k_cache, *v_cache;
+  const void *conv_in, *rec_in;
+  void *conv_out, *rec_out;
+} XbLayerState;
+
+typedef struct XbStepArgs {
+  int32_t batch;                      /* B, 1..8 */
+  const int64_t *input_ids;           /* device [B], or NULL to pass host_ids by value */
+  const int64_t *cache_position;      /* device [B], or NULL to pass host_positions by value */
+  int64_t host_ids[XB_MAX_BATCH];     /* used when input_ids == NULL (launch parameters, no copy) */
+  int64_t host_positions[XB_MAX_BATCH];
+  int32_t kv_lengths[XB_MAX_BATCH];   /* host values: populated length after this call */
+  int32_t query_lengths[XB_MAX_BATCH];/* host values: 0 (empty row) or 1 */
+  XbLayerState layers[XB_MAX_LAYERS];
+  void *logits;                       /* device bf16 [B, vocab] */
+  int64_t *next_tokens;               /* device int64 [B] or NULL: argmax of each logits row */
+} XbStepArgs;
+
+typedef struct XbModel XbModel;
+
+/* Build a device-side plan for one model: validates geometry, uploads the pointer table and
+ * the RoPE inverse frequencies (computed exactly as the HF rotary embedding does). */
+int xb_model_create(const XbGeometry *geometry, const XbModelWeights *weights, XbModel **model);
+int xb_model_destroy(XbModel *model);
+
+/* Bytes of device scratch one xb_decode_step of up to max_batch rows needs. */
+int xb_decode_workspace_bytes(const XbModel *model, int32_t max_batch, size_t *bytes);
+
+/* One decode step (T == 1) of B rows, one persistent kernel launch on `stream`.
+ * `workspace` must be zeroed once before first use (xb_workspace_init) and not shared by
+ * steps that overlap on the GPU. */
+int xb_workspace_init(void *workspace, size_t workspace_bytes, void *stream);
+int xb_decode_step(const XbModel *model, const XbStepArgs *args, void *workspace,
+                   size_t workspace_bytes, void *stream);
+
+/* Synchronises `stream` and returns XB_ERR_DEVICE if a kernel using `workspace` reported a
+ * device-side error since the last call (and clears it). */
+int xb_workspace_check(void *workspace, void *stream, int32_t *device_error);
+
+/* Host-only helper: the HF default RoPE inverse frequencies 1 / theta^(2i / rotary_dim) in fp32
+ * (transformers Qwen3_5TextRotaryEmbedding.compute_default_rope_parameters, as loaded by
+ * compiler/qwen35/model.py:41 and compiler/qwen3/model.py:16-26). */
+int xb_rope_inv_freq(float theta, int32_t rotary_dim, float *out);
+
+const char *xb_last_error(void);
+int xb_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XINFER_B200_H */

@@ -1,0 +1,263 @@
+"""Parity of the CUDA decode megakernel (through the C ABI) with the CPU oracle and with the
+golden fixtures made from the reference's own step.
+
+Tolerances are the north-star bar: bf16 logits max-abs <= 2e-2 and cosine >= 0.9999 per step;
+recurrent / conv state relative L2 <= 1e-2; greedy argmax of the kernel equals torch.argmax of
+the kernel's own logits exactly. KV slot writes are bf16 roundings of fp32 GEMV sums whose
+reduction order differs from the reference's GEMM library, so the test reports the bitwise
+fraction and bounds it, and checks exactly that no slot outside [position] was written.
+"""
+
+from pathlib import Path
+
+import pytest
+import torch
+
+from oracle import qwen_step as O
+from xinfer_b200 import configs, synthetic
+from xinfer_b200.engine import Engine, Runner
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_MAX_ABS = 2e-2
+LOGIT_COS = 0.9999
+STATE_REL = 1e-2
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+_MODELS = {}
+
+
+def model(name, capacity, device, jitter=0.1, seed=0):
+    key = (name, capacity, jitter, seed)
+    if key not in _MODELS:
+        g = configs.get(name)
+        sd = synthetic.make_state_dict(g, seed=seed, jitter=jitter)
+        eng = Engine(g, {k: v.to(device) for k, v in sd.items()}, capacity=capacity, device=device)
+        _MODELS[key] = (g, sd, LazyWeights(sd), eng)
+    return _MODELS[key]
+
+
+class LazyWeights(dict):
+    """fp32 oracle weights, converted on first use (full-size models only need them on demand)."""
+
+    def __init__(self, sd):
+        super().__init__()
+        self.sd = sd
+
+    def __missing__(self, key):
+        value = self.sd[key].float()
+        self[key] = value
+        return value
+
+    def get(self, key, default=None):
+        return self[key] if key in self.sd else default
+
+
+def check_logits(got, want, where):
+    got, want = got.float().cpu(), want.float().cpu()
+    err = (got - want).abs().max().item()
+    cos = O.cosine(got, want)
+    assert err <= LOGIT_MAX_ABS and cos >= LOGIT_COS, f"{where}: max abs {err}, cosine {cos}"
+
+
+def run_schedule_gpu(eng, g, schedule, device, rows_alloc=8):
+    """Drive Engine.decode_step (the reference decode ABI) over a row schedule."""
+    rows = len(schedule[0])
+    full = eng.allocate_state()
+    state = [t.narrow(0, 0, rows) for t in full]
+    positions = [0] * rows
+    logits_all, tokens_all = [], []
+    for tokens in schedule:
+        ids = torch.tensor([[t[0] if t else 0] for t in tokens], dtype=torch.int64, device=device)
+        pos = torch.tensor([[p] for p in positions], dtype=torch.int64, device=device)
+        kv = torch.tensor([positions[r] + len(tokens[r]) for r in range(rows)], dtype=torch.int32)
+        q = torch.tensor([len(t) for t in tokens], dtype=torch.int32)
+        nxt = torch.empty(rows, dtype=torch.int64, device=device)
+        out = eng.decode_step(ids, pos, state, kv, q, next_tokens=nxt)
+        if isinstance(out, tuple):
+            logits, *fresh = out
+            state = list(fresh)
+        else:
+            logits = out
+        eng.check_device_error()
+        logits_all.append(logits.clone())
+        tokens_all.append(nxt.clone())
+        for r in range(rows):
+            positions[r] += len(tokens[r])
+    return torch.stack(logits_all), torch.stack(tokens_all), state, full
+
+
+def run_schedule_oracle(g, W, schedule, capacity):
+    rows = len(schedule[0])
+    state = O.allocate_state(g, capacity, rows=rows)
+    positions = [0] * rows
+    out = []
+    for tokens in schedule:
+        ids = [t[0] if t else 0 for t in tokens]
+        kv = [positions[r] + len(tokens[r]) for r in range(rows)]
+        q = [len(t) for t in tokens]
+        logits, state = O.decode_step(g, W, ids, positions[:], state, kv, q)
+        out.append(logits)
+        for r in range(rows):
+            positions[r] += len(tokens[r])
+    return torch.stack(out), state
+
+
+def schedule_single(g, steps, seed=3):
+    gen = torch.Generator().manual_seed(seed)
+    return [[[int(torch.randint(0, g.vocab, (1,), generator=gen))]] for _ in range(steps)]
+
+
+def schedule_batch(g, seed=5):
+    gen = torch.Generator().manual_seed(seed)
+    active = [(1, 1, 1, 1), (1, 0, 1, 1), (1, 1, 0, 1), (0, 1, 1, 1), (1, 1, 1, 0), (1, 0, 0, 1)]
+    return [[[int(torch.randint(0, g.vocab, (1,), generator=gen))] if a else [] for a in row]
+            for row in active]
+
+
+@pytest.mark.parametrize("name", ["qwen3-tiny", "qwen3.5-tiny", "qwen3.5-tiny-hv32"])
+def test_single_row_matches_oracle(name, cuda_device):
+    g, sd, W, eng = model(name, 16, cuda_device)
+    sched = schedule_single(g, 10)
+    got, toks, state, _ = run_schedule_gpu(eng, g, sched, cuda_device)
+    want, ostate = run_schedule_oracle(g, W, sched, 16)
+    for s in range(len(sched)):
+        check_logits(got[s, 0], want[s, 0], f"{name} step {s}")
+        assert int(toks[s, 0]) == int(torch.argmax(got[s, 0].float())), "fused argmax"
+    for i, (a, b) in enumerate(zip(state, ostate)):
+        a = a.float().cpu()
+        b = b.float()
+        if g.is_delta(i // 2):
+            assert O.rel_l2(a, b) <= STATE_REL, f"state {i}"
+        else:
+            n = len(sched)
+            assert O.rel_l2(a[:, :, :n], b[:, :, :n]) <= STATE_REL, f"kv {i}"
+            assert torch.count_nonzero(a[:, :, n:]) == 0, "KV written outside the appended slots"
+
+
+@pytest.mark.parametrize("name", ["qwen3-tiny", "qwen3.5-tiny"])
+def test_ragged_batch_with_empty_rows(name, cuda_device):
+    g, sd, W, eng = model(name, 16, cuda_device)
+    sched = schedule_batch(g)
+    got, toks, state, full = run_schedule_gpu(eng, g, sched, cuda_device)
+    want, ostate = run_schedule_oracle(g, W, sched, 16)
+    for s, tokens in enumerate(sched):
+        for r, t in enumerate(tokens):
+            if t:
+                check_logits(got[s, r], want[s, r], f"{name} step {s} row {r}")
+                assert int(toks[s, r]) == int(torch.argmax(got[s, r].float()))
+            else:
+                assert torch.count_nonzero(got[s, r]) == 0, "empty rows return zero logits"
+    # rows >= B of the 8-row allocation are never touched
+    rows = len(sched[0])
+    for t in full:
+        assert torch.count_nonzero(t[rows:]) == 0
+
+
+def test_empty_row_keeps_state_bitwise(cuda_device):
+    g, sd, W, eng = model("qwen3.5-tiny", 16, cuda_device)
+    full = eng.allocate_state()
+    gen = torch.Generator(device=cuda_device).manual_seed(1)
+    for t in full:
+        t.copy_(torch.randn(t.shape, generator=gen, device=cuda_device).to(t.dtype) * 0.1)
+    state = [t.narrow(0, 0, 2) for t in full]
+    before = [t.clone() for t in state]
+    ids = torch.tensor([[3], [0]], dtype=torch.int64, device=cuda_device)
+    pos = torch.tensor([[5], [7]], dtype=torch.int64, device=cuda_device)
+    out = eng.decode_step(ids, pos, state, torch.tensor([6, 7], dtype=torch.int32),
+                          torch.tensor([1, 0], dtype=torch.int32))
+    eng.check_device_error()
+    logits, *fresh = out
+    assert torch.count_nonzero(logits[1]) == 0
+    for i, (a, b, inp) in enumerate(zip(fresh, before, state)):
+        if g.is_delta(i // 2):
+            assert torch.equal(inp, b), "inputs of replace state are unmodified"
+            assert torch.equal(a[1], b[1]), "empty row keeps its replacement state"
+            assert a.data_ptr() != inp.data_ptr()
+        else:
+            assert a.data_ptr() == inp.data_ptr(), "KV outputs alias the inputs"
+            assert torch.equal(a[1], b[1]), "empty row KV untouched"
+            changed = (a[0] != b[0]).any(dim=-1)  # [H, C]
+            assert not changed[:, :5].any() and not changed[:, 6:].any(), "only slot 5 written"
+
+
+@pytest.mark.parametrize("name", ["qwen3.5-tiny", "qwen3-tiny"])
+def test_long_prefix_split_kv(name, cuda_device):
+    """One step over a 3000-slot random prefix: exercises the split-KV partials and combine."""
+    cap = 4096
+    g, sd, W, eng = model(name, cap, cuda_device)
+    full = eng.allocate_state()
+    gen = torch.Generator().manual_seed(11)
+    cpu_state = []
+    for t in full:
+        v = (torch.randn(t.shape, generator=gen) * 0.5).to(t.dtype)
+        t.copy_(v)
+        cpu_state.append(v[:1].clone())
+    state = [t.narrow(0, 0, 1) for t in full]
+    L = 3000
+    ids = torch.tensor([[42]], dtype=torch.int64, device=cuda_device)
+    pos = torch.tensor([[L - 1]], dtype=torch.int64, device=cuda_device)
+    nxt = torch.empty(1, dtype=torch.int64, device=cuda_device)
+    out = eng.decode_step(ids, pos, state, torch.tensor([L], dtype=torch.int32),
+                          torch.tensor([1], dtype=torch.int32), next_tokens=nxt)
+    eng.check_device_error()
+    logits = out[0] if isinstance(out, tuple) else out
+    want, _ = O.decode_step(g, W, [42], [L - 1], cpu_state, [L], [1])
+    check_logits(logits[0], want[0], f"{name} L={L}")
+    assert int(nxt[0]) == int(torch.argmax(logits[0].float()))
+
+
+def test_runner_in_place_matches_replace_path(cuda_device):
+    g, sd, W, eng = model("qwen3.5-tiny", 16, cuda_device)
+    sched = schedule_single(g, 6, seed=9)
+    ref, _, _, _ = run_schedule_gpu(eng, g, sched, cuda_device)
+    runner = Runner(eng)
+    for s, tokens in enumerate(sched):
+        logits = runner.step(tokens[0])
+        assert torch.equal(logits[0], ref[s, 0]), f"in-place step {s} differs from replace step"
+
+
+def test_deterministic(cuda_device):
+    g, sd, W, eng = model("qwen3.5-tiny", 16, cuda_device)
+    sched = schedule_single(g, 4, seed=2)
+    a = run_schedule_gpu(eng, g, sched, cuda_device)[0]
+    b = run_schedule_gpu(eng, g, sched, cuda_device)[0]
+    assert torch.equal(a, b)
+
+
+def test_non_default_stream(cuda_device):
+    g, sd, W, eng = model("qwen3-tiny", 16, cuda_device)
+    sched = schedule_single(g, 3, seed=4)
+    ref = run_schedule_gpu(eng, g, sched, cuda_device)[0]
+    side = torch.cuda.Stream(cuda_device)
+    with torch.cuda.stream(side):
+        got = run_schedule_gpu(eng, g, sched, cuda_device)[0]
+    side.synchronize()
+    assert torch.equal(got, ref)
+
+
+@pytest.mark.parametrize("fixture", sorted(p.stem for p in GOLDEN.glob("*.pt")))
+def test_matches_reference_fixtures(fixture, cuda_device):
+    fx = torch.load(GOLDEN / f"{fixture}.pt", weights_only=False)
+    g, sd, W, eng = model(fx["config"], fx["capacity"], cuda_device, jitter=fx["jitter"], seed=fx["seed"])
+    got, toks, state, _ = run_schedule_gpu(eng, g, fx["schedule"], cuda_device)
+    summary = fx["logits_summary"]
+    for s, tokens in enumerate(fx["schedule"]):
+        for r, t in enumerate(tokens):
+            if not t:
+                assert torch.count_nonzero(got[s, r]) == 0
+                continue
+            if fx["logits"] is not None:
+                check_logits(got[s, r], fx["logits"][s, r], f"{fixture} step {s} row {r}")
+            else:
+                idx = summary["top_indices"][s, r]
+                vals = got[s, r].float().cpu()[idx]
+                err = (vals - summary["top_values"][s, r].float()).abs().max().item()
+                assert err <= LOGIT_MAX_ABS, f"{fixture} step {s}: top-32 logits differ by {err}"
+                sl = got[s, r, ::97].float().cpu()
+                ref = summary["stride_slice"][s, r].float()
+                assert O.cosine(sl, ref) >= LOGIT_COS
+                assert (sl - ref).abs().max().item() <= LOGIT_MAX_ABS
+    for i, smp in enumerate(fx["state_sample"]):
+        a = state[i].reshape(-1)[smp["index"].long().to(cuda_device)].float().cpu()
+        assert O.rel_l2(a, smp["value"].float()) <= STATE_REL, f"{fixture} state {i}"

@@ -1,0 +1,1353 @@
+// Persistent sm_100a decode megakernel for the Qwen3 / Qwen3.5 decode step (T == 1, B <= 8).
+//
+// One cooperative launch per step, one CTA per SM. Each CTA runs two roles:
+//   * a producer warp that streams this CTA's share of every weight matrix of the step, in
+//     consumption order, through a ring of 32 KB shared-memory slots with 1-D bulk copies (TMA,
+//     cp.async.bulk, completion on mbarriers). Weights do not depend on activations, so the
+//     producer runs ahead across stage boundaries and keeps HBM busy while the consumers wait at
+//     grid barriers;
+//   * eight consumer warps that run the stages of the layer loop:
+//       DeltaNet layer : in_proj GEMV -> conv/delta-rule -> gated norm + out_proj -> gate/up -> down
+//       attention layer: q/k/v GEMV -> norm/RoPE/KV append/split-KV partials -> combine
+//                        -> o_proj -> gate/up -> down
+//       final          : final norm + lm_head GEMV with fused argmax.
+//     Stages are separated by a grid-wide barrier (bounded spin). RMSNorms are recomputed by every
+//     CTA from the residual stream in its stage prologue; SiLU*mul and residual adds are fused into
+//     GEMV epilogues.
+// Rounding points follow the reference step (bf16 tensors between ops, fp32 inside each op):
+//   compiler/qwen35/model.py:162-183, compiler/qwen35/adapters/{attention.py:39-63,delta.py:32-49},
+//   compiler/qwen35/kernels/recurrent.py:20-124, compiler/qwen3/model.py:70-95,
+//   compiler/qwen3/adapters/attention.py:41-62, compiler/common/kernels/kv_cache.py:8-42,
+//   compiler/common/kernels/attention.cpp:14-79.
+
+#include "xb_device.cuh"
+#include "xinfer_b200.h"
+
+#include <cuda.h>
+#include <cstdio>
+#include <cstring>
+#include <cmath>
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace xb {
+
+constexpr int kWarps = 8;                 // consumer warps
+constexpr int kCT = kWarps * 32;          // consumer threads
+constexpr int kThreads = kCT + 32;        // + producer warp
+constexpr int kSlot = 32768;              // ring slot bytes
+constexpr int kMaxSlots = 8;
+constexpr int kHdrBytes = 256;
+constexpr int kRedFloats = 1024;
+constexpr int kUOffset = kHdrBytes + kRedFloats * 4;  // 4352, 128-aligned
+constexpr int kSmemLimit = 232448;                     // 227 KB opt-in per CTA
+
+// control words in the workspace (each on its own 128-byte line)
+enum { CTL_COUNT = 0, CTL_GEN = 32, CTL_ERR = 64, CTL_DONE = 96, CTL_WORDS = 128 };
+// device error codes
+enum { DERR_BARRIER = 1, DERR_RING_FULL = 2, DERR_RING_EMPTY = 3, DERR_TOKEN = 4, DERR_DRAIN = 5 };
+
+enum Stage {
+  ST_IN_DELTA = 0, ST_OUT_DELTA, ST_QKV, ST_O, ST_GATEUP, ST_DOWN, ST_LMHEAD
+};
+enum Epi { EPI_STORE = 0, EPI_RESID, EPI_GATEUP, EPI_LOGITS };
+
+struct StepParams {
+  int family, L, H, I, V, HQ, HKV, D, RD, HK, HV, DK, CW, C, rows_alloc;
+  float eps, dk_scale, att_scale;
+  int pstride, splits, ncta, nslots, ubytes, B;
+  int kv_len[XB_MAX_BATCH], q_len[XB_MAX_BATCH];
+  unsigned long long delta_mask;
+  const XbLayerWeights *layers;
+  const bf16 *embed, *final_norm, *lm_head;
+  const float *inv_freq;
+  const int64_t *ids, *pos;  // device arrays, or NULL: use hid / hpos
+  long long hid[XB_MAX_BATCH], hpos[XB_MAX_BATCH];
+  void *sa[XB_MAX_LAYERS], *sb[XB_MAX_LAYERS], *sc[XB_MAX_LAYERS], *sd[XB_MAX_LAYERS];
+  bf16 *logits;
+  int64_t *tokens;
+  unsigned *ctrl;
+  bf16 *h, *proj, *core, *att_out, *act;
+  float *ssq, *att_o, *att_ml, *am_v;
+  int *am_i;
+};
+
+struct SmemHdr {
+  uint64_t full[kMaxSlots];
+  uint64_t empty[kMaxSlots];
+  int abort;
+  int is_last;
+};
+static_assert(sizeof(SmemHdr) <= kHdrBytes, "header");
+
+// One GEMV stage: logical rows [0, N) over up to four row segments (concatenated), or a
+// gate/up pair (paired: logical row i is row i of seg[0] and row i of seg[1]).
+struct Gemv {
+  const bf16 *seg[4];
+  int seg_rows[4];
+  int nseg;
+  int K, N;
+  bool paired;
+  int stage;
+};
+
+__device__ __forceinline__ long long token_id(const StepParams &p, int b) {
+  return p.ids ? (long long)p.ids[b] : p.hid[b];
+}
+__device__ __forceinline__ long long position(const StepParams &p, int b) {
+  return p.pos ? (long long)p.pos[b] : p.hpos[b];
+}
+
+__device__ __forceinline__ bool is_delta(const StepParams &p, int l) {
+  return (p.delta_mask >> l) & 1ull;
+}
+
+__device__ __forceinline__ Gemv make_gemv(const StepParams &p, int l, int stage) {
+  Gemv g;
+  g.nseg = 1;
+  g.paired = false;
+  g.stage = stage;
+  for (int i = 0; i < 4; ++i) { g.seg[i] = nullptr; g.seg_rows[i] = 0; }
+  if (stage == ST_LMHEAD) {
+    g.seg[0] = p.lm_head; g.seg_rows[0] = p.V; g.K = p.H; g.N = p.V;
+    return g;
+  }
+  const XbLayerWeights &w = p.layers[l];
+  switch (stage) {
+  case ST_IN_DELTA: {
+    const int key = p.HK * p.DK, val = p.HV * p.DK;
+    g.nseg = 4;
+    g.seg[0] = (const bf16 *)w.in_qkv; g.seg_rows[0] = 2 * key + val;
+    g.seg[1] = (const bf16 *)w.in_z;   g.seg_rows[1] = val;
+    g.seg[2] = (const bf16 *)w.in_b;   g.seg_rows[2] = p.HV;
+    g.seg[3] = (const bf16 *)w.in_a;   g.seg_rows[3] = p.HV;
+    g.K = p.H;
+    break;
+  }
+  case ST_OUT_DELTA:
+    g.seg[0] = (const bf16 *)w.out_proj; g.seg_rows[0] = p.H; g.K = p.HV * p.DK;
+    break;
+  case ST_QKV: {
+    const int qrows = p.HQ * p.D * (p.family == XB_FAMILY_QWEN35 ? 2 : 1);
+    g.nseg = 3;
+    g.seg[0] = (const bf16 *)w.q_proj; g.seg_rows[0] = qrows;
+    g.seg[1] = (const bf16 *)w.k_proj; g.seg_rows[1] = p.HKV * p.D;
+    g.seg[2] = (const bf16 *)w.v_proj; g.seg_rows[2] = p.HKV * p.D;
+    g.K = p.H;
+    break;
+  }
+  case ST_O:
+    g.seg[0] = (const bf16 *)w.o_proj; g.seg_rows[0] = p.H; g.K = p.HQ * p.D;
+    break;
+  case ST_GATEUP:
+    g.nseg = 2; g.paired = true;
+    g.seg[0] = (const bf16 *)w.gate; g.seg_rows[0] = p.I;
+    g.seg[1] = (const bf16 *)w.up;   g.seg_rows[1] = p.I;
+    g.K = p.H;
+    g.N = p.I;
+    return g;
+  case ST_DOWN:
+    g.seg[0] = (const bf16 *)w.down; g.seg_rows[0] = p.H; g.K = p.I;
+    break;
+  }
+  g.N = 0;
+  for (int i = 0; i < g.nseg; ++i) g.N += g.seg_rows[i];
+  return g;
+}
+
+__device__ __forceinline__ int tile_rows(const Gemv &g) {
+  return kSlot / (g.K * 2 * (g.paired ? 2 : 1));
+}
+__device__ __forceinline__ void cta_range(int N, int cta, int ncta, int &lo, int &hi) {
+  lo = (int)(((long long)N * cta) / ncta);
+  hi = (int)(((long long)N * (cta + 1)) / ncta);
+}
+
+// ------------------------------------------------------------------------------------------
+// Producer role: lane 0 of the last warp issues every weight tile of this CTA, in order.
+// ------------------------------------------------------------------------------------------
+struct Producer {
+  const StepParams &p;
+  SmemHdr *hdr;
+  char *ring;
+  uint64_t policy;
+  int slot = 0;
+  unsigned phase = 0;
+  int issued = 0;
+  bool stop = false;
+
+  __device__ Producer(const StepParams &p_, SmemHdr *h, char *r) : p(p_), hdr(h), ring(r) {
+    policy = policy_evict_first();
+  }
+
+  __device__ bool acquire() {
+    // Wait until the consumers released this slot AND the previous copy into it has landed
+    // (the second condition only matters after an abort, when consumers release unread slots).
+    uint64_t t0 = 0;
+    unsigned spins = 0;
+    while (!mbar_try_wait(&hdr->empty[slot], phase ^ 1u) ||
+           (issued >= p.nslots && !mbar_try_wait(&hdr->full[slot], phase ^ 1u))) {
+      if ((++spins & 63u) == 0) {
+        if (ld_volatile(p.ctrl + CTL_ERR)) return false;
+        const uint64_t t = globaltimer();
+        if (t0 == 0) t0 = t;
+        else if (t - t0 > 2 * kWaitLimitNs) {
+          atomicCAS(p.ctrl + CTL_ERR, 0u, (unsigned)DERR_RING_EMPTY);
+          return false;
+        }
+      }
+    }
+    return true;
+  }
+
+  __device__ void gemv(int l, int stage) {
+    if (stop) return;
+    const Gemv g = make_gemv(p, l, stage);
+    int lo, hi;
+    cta_range(g.N, blockIdx.x, p.ncta, lo, hi);
+    const int R = tile_rows(g);
+    const unsigned rowb = (unsigned)g.K * 2u;
+    for (int r0 = lo; r0 < hi; r0 += R) {
+      const int n = min(R, hi - r0);
+      if (!acquire()) { stop = true; return; }
+      char *dst = ring + (size_t)slot * kSlot;
+      uint64_t *bar = &hdr->full[slot];
+      if (g.paired) {
+        const unsigned bytes = (unsigned)n * rowb;
+        mbar_arrive_expect_tx(bar, 2u * bytes);
+        bulk_g2s(dst, g.seg[0] + (size_t)r0 * g.K, bytes, bar, policy);
+        bulk_g2s(dst + bytes, g.seg[1] + (size_t)r0 * g.K, bytes, bar, policy);
+      } else {
+        mbar_arrive_expect_tx(bar, (unsigned)n * rowb);
+        int base = 0;
+        for (int s = 0; s < g.nseg; ++s) {
+          const int a = max(r0, base), b = min(r0 + n, base + g.seg_rows[s]);
+          if (a < b)
+            bulk_g2s(dst + (size_t)(a - r0) * rowb, g.seg[s] + (size_t)(a - base) * g.K,
+                     (unsigned)(b - a) * rowb, bar, policy);
+          base += g.seg_rows[s];
+        }
+      }
+      ++issued;
+      if (++slot == p.nslots) { slot = 0; phase ^= 1u; }
+    }
+  }
+  __device__ void delta(int) {}
+  __device__ void attn(int) {}
+  __device__ void comb(int) {}
+};
+
+// ------------------------------------------------------------------------------------------
+// Consumer role
+// ------------------------------------------------------------------------------------------
+template <int NB> struct Consumer {
+  const StepParams &p;
+  SmemHdr *hdr;
+  float *red;     // kRedFloats
+  char *U;        // union region: GEMV activations / attention scratch
+  char *ring;
+  int tid, warp, lane;
+  int slot = 0;
+  unsigned phase = 0;
+  bool first = true;      // first stage of the step needs no barrier
+  bool h_ready = false;   // residual stream in p.h (false: still the embedding rows)
+  // running argmax for the lm_head stage (lane b keeps batch row b)
+  float am_v = -INFINITY;
+  int am_i = 0x7fffffff;
+
+  __device__ Consumer(const StepParams &p_, SmemHdr *h, float *r, char *u, char *rg)
+      : p(p_), hdr(h), red(r), U(u), ring(rg) {
+    tid = threadIdx.x;
+    warp = tid >> 5;
+    lane = tid & 31;
+  }
+
+  __device__ __forceinline__ void csync() { named_sync<kCT>(1); }
+
+  // Abort rules: every consumer thread always executes the same sequence of named barriers.
+  // An abort (device error word set anywhere in the grid) only skips waits and GEMV tiles.
+  __device__ __forceinline__ bool aborted() const {
+    return *reinterpret_cast<volatile int *>(&hdr->abort) != 0;
+  }
+  __device__ void set_abort(unsigned code) {
+    atomicCAS(p.ctrl + CTL_ERR, 0u, code);
+    *reinterpret_cast<volatile int *>(&hdr->abort) = 1;
+  }
+
+  __device__ void grid_sync() {
+    csync();
+    if (tid == 0 && !aborted()) {
+      unsigned *ctrl = p.ctrl;
+      const unsigned gen = ld_acquire(ctrl + CTL_GEN);
+      __threadfence();
+      const unsigned prev = atomicAdd(ctrl + CTL_COUNT, 1u);
+      if (prev == (unsigned)p.ncta - 1u) {
+        atomicExch(ctrl + CTL_COUNT, 0u);
+        __threadfence();
+        st_release(ctrl + CTL_GEN, gen + 1u);
+      } else {
+        uint64_t t0 = globaltimer();
+        unsigned spins = 0;
+        while (ld_acquire(ctrl + CTL_GEN) == gen) {
+          if ((++spins & 255u) == 0) {
+            if (ld_volatile(ctrl + CTL_ERR)) break;
+            if (globaltimer() - t0 > kWaitLimitNs) {
+              atomicCAS(ctrl + CTL_ERR, 0u, (unsigned)DERR_BARRIER);
+              break;
+            }
+          }
+        }
+      }
+      __threadfence();
+      if (ld_volatile(ctrl + CTL_ERR)) *reinterpret_cast<volatile int *>(&hdr->abort) = 1;
+    }
+    csync();
+  }
+
+  __device__ void stage_begin() {
+    if (first) { first = false; return; }
+    grid_sync();
+  }
+
+  __device__ const char *wait_full() {
+    if (aborted()) return nullptr;
+    uint64_t t0 = 0;
+    unsigned spins = 0;
+    while (!mbar_try_wait(&hdr->full[slot], phase)) {
+      if ((++spins & 63u) == 0) {
+        if (aborted()) return nullptr;
+        if (ld_volatile(p.ctrl + CTL_ERR)) {
+          *reinterpret_cast<volatile int *>(&hdr->abort) = 1;
+          return nullptr;
+        }
+        const uint64_t t = globaltimer();
+        if (t0 == 0) t0 = t;
+        else if (t - t0 > kWaitLimitNs) {
+          set_abort(DERR_RING_FULL);
+          return nullptr;
+        }
+      }
+    }
+    return ring + (size_t)slot * kSlot;
+  }
+  __device__ void release() {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&hdr->empty[slot]);
+    if (++slot == p.nslots) { slot = 0; phase ^= 1u; }
+  }
+
+  // Residual-stream row b, element e (embedding row before the first residual update).
+  __device__ __forceinline__ float hval(int b, int e) const {
+    if (!h_ready) {
+      const long long id = token_id(p, b);
+      return bf(p.embed[(size_t)id * p.H + e]);
+    }
+    return bf(ldcg_bf(p.h + (size_t)b * p.H + e));
+  }
+
+  // RMSNorm of the residual stream into the activation buffer (bf16 [NB][H]).
+  //  Qwen3   : w * bf16(x * rsqrt(mean(x^2) + eps))        (HF Qwen3RMSNorm)
+  //  Qwen3.5 : bf16(x * rsqrt(mean(x^2) + eps) * (1 + w))   (HF Qwen3_5RMSNorm)
+  __device__ void norm_prologue(const bf16 *w) {
+    bf16 *act = reinterpret_cast<bf16 *>(U);
+    const int H = p.H;
+    float ss[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      ss[b] = 0.f;
+      if (b < p.B)
+        for (int e = tid; e < H; e += kCT) { const float x = hval(b, e); ss[b] = fmaf(x, x, ss[b]); }
+      ss[b] = warp_sum(ss[b]);
+    }
+    if (lane == 0)
+#pragma unroll
+      for (int b = 0; b < NB; ++b) red[warp * NB + b] = ss[b];
+    csync();
+    const bool q35 = p.family == XB_FAMILY_QWEN35;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      if (b < p.B) {
+        float tot = 0.f;
+        for (int i = 0; i < kWarps; ++i) tot += red[i * NB + b];
+        const float r = rsqrtf(tot / (float)H + p.eps);
+        for (int e = tid; e < H; e += kCT) {
+          const float x = hval(b, e), wv = bf(w[e]);
+          const float y = q35 ? rbf(x * r * (1.f + wv)) : rbf(wv * rbf(x * r));
+          act[b * H + e] = tobf(y);
+        }
+      } else {
+        for (int e = tid; e < H; e += kCT) act[b * H + e] = tobf(0.f);
+      }
+    }
+    csync();
+  }
+
+  // Copy a bf16 scratch vector [B][K] (stride ld) produced this launch into the activations.
+  __device__ void copy_prologue(const bf16 *src, int K, int ld) {
+    bf16 *act = reinterpret_cast<bf16 *>(U);
+    const int n8 = K / 8;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      uint4 *dst = reinterpret_cast<uint4 *>(act + b * K);
+      for (int j = tid; j < n8; j += kCT)
+        dst[j] = (b < p.B) ? ldcg_u4(src + (size_t)b * ld + j * 8) : make_uint4(0, 0, 0, 0);
+    }
+    csync();
+  }
+
+  // Gated RMSNorm of the DeltaNet core output (HF Qwen3_5RMSNormGated, as called in
+  // compiler/qwen35/adapters/delta.py:46-47): y = bf16( bf16(w * bf16(x * r)) * silu(z) ).
+  __device__ void gated_norm_prologue(const bf16 *w) {
+    bf16 *act = reinterpret_cast<bf16 *>(U);
+    const int K = p.HV * p.DK, DK = p.DK;
+    const int zoff = 2 * p.HK * p.DK + p.HV * p.DK;
+    float *rs = red;  // [NB][HV] inverse rms
+    for (int i = tid; i < NB * p.HV; i += kCT) {
+      const int b = i / p.HV, h = i % p.HV;
+      float r = 0.f;
+      if (b < p.B) {
+        float tot = 0.f;
+        for (int t = 0; t < 8; ++t) tot += ldcg_f(p.ssq + ((size_t)b * p.HV + h) * 8 + t);
+        r = rsqrtf(tot / (float)DK + p.eps);
+      }
+      rs[i] = r;
+    }
+    csync();
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      for (int e = tid; e < K; e += kCT) {
+        float y = 0.f;
+        if (b < p.B) {
+          const float x = bf(ldcg_bf(p.core + (size_t)b * K + e));
+          const float r = rs[b * p.HV + e / DK];
+          const float n = rbf(bf(w[e % DK]) * rbf(x * r));
+          const float z = bf(ldcg_bf(p.proj + (size_t)b * p.pstride + zoff + e));
+          const float s = z / (1.f + expf(-z));
+          y = rbf(n * s);
+        }
+        act[b * K + e] = tobf(y);
+      }
+    }
+    csync();
+  }
+
+  // Next conv window per channel: [conv[1], conv[2], conv[3], x] for active rows, unchanged for
+  // empty rows (recurrent.py:43-52). Runs after the barrier that ends the DeltaNet stage, when
+  // no CTA reads the old window any more; each element is read before it is overwritten.
+  __device__ void conv_state_update(int l) {
+    const int CH = (2 * p.HK + p.HV) * p.DK;
+    const uint2 *cin = reinterpret_cast<const uint2 *>(p.sa[l]);
+    uint2 *cout = reinterpret_cast<uint2 *>(p.sc[l]);
+    int lo, hi;
+    cta_range(p.B * CH, blockIdx.x, p.ncta, lo, hi);
+    for (int i = lo + tid; i < hi; i += kCT) {
+      const int b = i / CH, ch = i % CH;
+      const uint2 old = cin[i];
+      uint2 nw = old;
+      if (p.q_len[b] > 0) {
+        const bf16 xb = ldcg_bf(p.proj + (size_t)b * p.pstride + ch);
+        nw.x = (old.x >> 16) | (old.y << 16);
+        nw.y = (old.y >> 16) | ((uint32_t)__bfloat16_as_ushort(xb) << 16);
+      }
+      cout[i] = nw;
+    }
+  }
+
+  // ---- GEMV tile loop ----------------------------------------------------------------------
+  __device__ void gemv(int l, int stage) {
+    stage_begin();
+    const Gemv g = make_gemv(p, l, stage);
+    const XbLayerWeights *w = (stage == ST_LMHEAD) ? nullptr : &p.layers[l];
+    int epi = EPI_STORE;
+    switch (stage) {
+    case ST_IN_DELTA:
+    case ST_QKV: norm_prologue((const bf16 *)w->input_norm); epi = EPI_STORE; break;
+    case ST_OUT_DELTA:
+      conv_state_update(l);
+      gated_norm_prologue((const bf16 *)w->gnorm);
+      epi = EPI_RESID;
+      break;
+    case ST_O: copy_prologue(p.att_out, g.K, p.HQ * p.D); epi = EPI_RESID; break;
+    case ST_GATEUP: norm_prologue((const bf16 *)w->post_norm); epi = EPI_GATEUP; break;
+    case ST_DOWN: copy_prologue(p.act, g.K, p.I); epi = EPI_RESID; break;
+    case ST_LMHEAD: norm_prologue(p.final_norm); epi = EPI_LOGITS; break;
+    }
+    const bf16 *act = reinterpret_cast<const bf16 *>(U);
+    int lo, hi;
+    cta_range(g.N, blockIdx.x, p.ncta, lo, hi);
+    const int R = tile_rows(g);
+    const int K = g.K, n8 = K / 8;
+    for (int r0 = lo; r0 < hi; r0 += R) {
+      const int n = min(R, hi - r0);
+      const char *slotp = wait_full();
+      for (int i = warp; slotp && i < n; i += kWarps) {
+        float acc[NB], acc2[NB];
+#pragma unroll
+        for (int b = 0; b < NB; ++b) { acc[b] = 0.f; acc2[b] = 0.f; }
+        const uint4 *w4 = reinterpret_cast<const uint4 *>(slotp + (size_t)i * K * 2);
+        const uint4 *u4 = reinterpret_cast<const uint4 *>(slotp + (size_t)(n + i) * K * 2);
+        for (int j = lane; j < n8; j += 32) {
+          float wf[8], uf[8];
+          unpack8(w4[j], wf);
+          if (g.paired) unpack8(u4[j], uf);
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            float xf[8];
+            unpack8(reinterpret_cast<const uint4 *>(act + b * K)[j], xf);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[b] = fmaf(wf[e], xf[e], acc[b]);
+            if (g.paired) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) acc2[b] = fmaf(uf[e], xf[e], acc2[b]);
+            }
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          acc[b] = warp_sum(acc[b]);
+          if (g.paired) acc2[b] = warp_sum(acc2[b]);
+        }
+        float v = acc[0], v2 = acc2[0];
+#pragma unroll
+        for (int b = 1; b < NB; ++b)
+          if (lane == b) { v = acc[b]; v2 = acc2[b]; }
+        if (lane < NB && lane < p.B) epilogue(epi, lane, r0 + i, v, v2);
+      }
+      release();
+    }
+    if (epi == EPI_RESID) h_ready = true;
+    if (epi == EPI_LOGITS) argmax_finish();
+  }
+
+  __device__ __forceinline__ void epilogue(int epi, int b, int row, float v, float v2) {
+    switch (epi) {
+    case EPI_STORE:
+      p.proj[(size_t)b * p.pstride + row] = tobf(v);
+      break;
+    case EPI_RESID: {
+      const float hv = hval(b, row);
+      p.h[(size_t)b * p.H + row] = tobf(hv + rbf(v));
+      break;
+    }
+    case EPI_GATEUP: {
+      const float gt = rbf(v), up = rbf(v2);
+      const float s = rbf(gt / (1.f + expf(-gt)));
+      p.act[(size_t)b * p.I + row] = tobf(s * up);
+      break;
+    }
+    case EPI_LOGITS: {
+      const float y = p.q_len[b] > 0 ? rbf(v) : 0.f;
+      p.logits[(size_t)b * p.V + row] = tobf(y);
+      if (argmax_better(y, row, am_v, am_i)) { am_v = y; am_i = row; }
+      break;
+    }
+    }
+  }
+
+  // Per-CTA argmax -> workspace; the last CTA to finish reduces all CTAs (ordered by rows).
+  __device__ void argmax_finish() {
+    float *sv = red;                       // [kWarps][NB]
+    int *si = reinterpret_cast<int *>(red + kWarps * NB);
+    if (lane < NB) { sv[warp * NB + lane] = am_v; si[warp * NB + lane] = am_i; }
+    csync();
+    if (tid < NB && tid < p.B) {
+      float bv = sv[tid];
+      int bi = si[tid];
+      for (int i = 1; i < kWarps; ++i)
+        if (argmax_better(sv[i * NB + tid], si[i * NB + tid], bv, bi)) {
+          bv = sv[i * NB + tid];
+          bi = si[i * NB + tid];
+        }
+      p.am_v[blockIdx.x * XB_MAX_BATCH + tid] = bv;
+      p.am_i[blockIdx.x * XB_MAX_BATCH + tid] = bi;
+    }
+    csync();
+    if (tid == 0) {
+      __threadfence();
+      const unsigned prev = atomicAdd(p.ctrl + CTL_DONE, 1u);
+      hdr->is_last = prev == (unsigned)p.ncta - 1u;
+    }
+    csync();
+    if (hdr->is_last) {
+      __threadfence();
+      if (tid < p.B && p.tokens) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int c = 0; c < p.ncta; ++c) {
+          const float v = ldcg_f(p.am_v + c * XB_MAX_BATCH + tid);
+          const int i = __ldcg(p.am_i + c * XB_MAX_BATCH + tid);
+          if (argmax_better(v, i, bv, bi)) { bv = v; bi = i; }
+        }
+        p.tokens[tid] = bi;
+      }
+      if (tid == 0) atomicExch(p.ctrl + CTL_DONE, 0u);
+    }
+  }
+
+  // ---- Gated DeltaNet recurrent step (compiler/qwen35/kernels/recurrent.py:20-124) ---------
+  // Work item = (row b, value head h, 16-column tile t of the 128x128 state).
+  __device__ void delta(int l) {
+    stage_begin();
+    const XbLayerWeights &w = p.layers[l];
+    const int HK = p.HK, HV = p.HV, DK = p.DK;
+    const int CH = (2 * HK + HV) * DK, CW = p.CW;
+    const int group = HV / HK;
+    const int tiles = DK / 16;
+    const int items = p.B * HV * tiles;
+    const bf16 *cw = (const bf16 *)w.conv_w;
+    float *qk = red;              // [2*DK]  (q | k)
+    float *vv = red + 2 * DK;     // [16]
+    float *part = red + 2 * DK + 16;   // [kWarps][16]
+    float *misc = red + 2 * DK + 16 + kWarps * 16;  // [8]
+    const bf16 *conv_in_all = (const bf16 *)p.sa[l];
+    const float *rec_in_all = (const float *)p.sb[l];
+    float *rec_out_all = (float *)p.sd[l];
+    for (int item = blockIdx.x; item < items; item += p.ncta) {
+      const int b = item / (HV * tiles);
+      const int h = (item / tiles) % HV;
+      const int t = item % tiles;
+      const int kh = h / group;
+      const bf16 *cin = conv_in_all + (size_t)b * CH * CW;
+      const float *S_in = rec_in_all + (((size_t)b * HV + h) * DK) * DK;
+      float *S_out = rec_out_all + (((size_t)b * HV + h) * DK) * DK;
+      // state thread mapping: col c, rows r0..r0+7
+      const int c = lane & 15;
+      const int rbase = warp * 16 + (lane >> 4) * 8;
+      const int col = t * 16 + c;
+      if (p.q_len[b] == 0) {
+        // Empty row: replacement state equals the input state (a no-op when in place).
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          S_out[(size_t)(rbase + i) * DK + col] = S_in[(size_t)(rbase + i) * DK + col];
+        if (tid < 16) p.core[(size_t)b * HV * DK + h * DK + t * 16 + tid] = tobf(0.f);
+        if (tid == 0) p.ssq[((size_t)b * HV + h) * 8 + t] = 0.f;
+        continue;
+      }
+      const bf16 *x = p.proj + (size_t)b * p.pstride;
+      // causal conv (width 4) over [conv[1..3], x] + SiLU, rounded as recurrent.py:32-58.
+      // The updated conv window is written after the next grid barrier (conv_state_update), so
+      // the state may be updated in place.
+      auto conv = [&](int ch) -> float {
+        const float h0 = bf(cin[ch * CW + 1]), h1 = bf(cin[ch * CW + 2]), h2 = bf(cin[ch * CW + 3]);
+        const float h3 = bf(ldcg_bf(x + ch));
+        float tot = 0.f;
+        tot = fmaf(h0, bf(cw[ch * CW + 0]), tot);
+        tot = fmaf(h1, bf(cw[ch * CW + 1]), tot);
+        tot = fmaf(h2, bf(cw[ch * CW + 2]), tot);
+        tot = fmaf(h3, bf(cw[ch * CW + 3]), tot);
+        const float v = rbf(tot);
+        return rbf(v * (1.f / (1.f + expf(-v))));
+      };
+      if (tid < 2 * DK) {
+        const int ch = tid < DK ? kh * DK + tid : (HK + kh) * DK + (tid - DK);
+        qk[tid] = conv(ch);
+      }
+      if (tid < 16) vv[tid] = conv((2 * HK + h) * DK + t * 16 + tid);
+      csync();
+      // L2 norms of q (warps 0-3) and k (warps 4-7)
+      {
+        const float x0 = qk[tid];
+        float s = warp_sum(x0 * x0);
+        if (lane == 0) part[warp] = s;
+      }
+      csync();
+      if (tid == 0) {
+        const float sq = part[0] + part[1] + part[2] + part[3];
+        const float sk = part[4] + part[5] + part[6] + part[7];
+        misc[0] = rsqrtf(sq + 1e-6f);
+        misc[1] = rsqrtf(sk + 1e-6f);
+        const float bb = bf(ldcg_bf(x + CH + HV * DK + h));
+        misc[2] = rbf(1.f / (1.f + expf(-bb)));  // beta
+        const float a = bf(ldcg_bf(x + CH + HV * DK + HV + h));
+        const float xx = a + bf(((const bf16 *)w.dt_bias)[h]);
+        const float sp = xx > 20.f ? xx : log1pf(expf(xx));
+        const float g = -expf(bf(((const bf16 *)w.a_log)[h])) * sp;
+        misc[3] = expf(g);  // decay
+      }
+      csync();
+      const float qs = misc[0], ks = misc[1], beta = misc[2], decay = misc[3];
+      const float qscale = p.dk_scale;
+      float S[8], kr[8], qr[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        S[i] = S_in[(size_t)(rbase + i) * DK + col];
+        kr[i] = qk[DK + rbase + i] * ks;
+        qr[i] = qk[rbase + i] * qs * qscale;
+      }
+      float pr = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { S[i] *= decay; pr = fmaf(S[i], kr[i], pr); }
+      pr += __shfl_xor_sync(0xffffffffu, pr, 16);
+      if (lane < 16) part[warp * 16 + lane] = pr;
+      csync();
+      float pred = 0.f;
+      for (int i = 0; i < kWarps; ++i) pred += part[i * 16 + c];
+      const float delta_c = (vv[c] - pred) * beta;
+      csync();  // part[] reused below
+      float o = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        S[i] = fmaf(kr[i], delta_c, S[i]);
+        o = fmaf(S[i], qr[i], o);
+        S_out[(size_t)(rbase + i) * DK + col] = S[i];
+      }
+      o += __shfl_xor_sync(0xffffffffu, o, 16);
+      if (lane < 16) part[warp * 16 + lane] = o;
+      csync();
+      if (tid < 16) {
+        float out = 0.f;
+        for (int i = 0; i < kWarps; ++i) out += part[i * 16 + tid];
+        const float ob = rbf(out);
+        p.core[(size_t)b * HV * DK + h * DK + t * 16 + tid] = tobf(ob);
+        float sq = ob * ob;
+#pragma unroll
+        for (int o2 = 8; o2; o2 >>= 1) sq += __shfl_xor_sync(0x0000ffffu, sq, o2);
+        if (tid == 0) p.ssq[((size_t)b * HV + h) * 8 + t] = sq;
+      }
+      csync();
+    }
+  }
+
+  // ---- attention: q/k norm, RoPE, KV append, split-KV partials ----------------------------
+  __device__ void attn(int l) {
+    stage_begin();
+    const XbLayerWeights &w = p.layers[l];
+    const int D = p.D, HQ = p.HQ, HKV = p.HKV, G = HQ / HKV, RD = p.RD;
+    const bool q35 = p.family == XB_FAMILY_QWEN35;
+    const int qrow = q35 ? 2 * D : D;
+    const int koff = HQ * qrow, voff = koff + HKV * D;
+    const int EPL = D / 32;  // elements per lane (4 or 8)
+    const int splits = p.splits;
+    const int items = p.B * HKV * splits;
+    float *qs = reinterpret_cast<float *>(U);        // [G][D]
+    float *kn = qs + G * D;                          // [D]
+    float *vn = kn + D;                              // [D]
+    float *mg = vn + D;                              // [kWarps][G][D+2]
+    bf16 *kc_all = (bf16 *)p.sa[l];
+    bf16 *vc_all = (bf16 *)p.sb[l];
+    const float scale = p.att_scale;
+    for (int item = blockIdx.x; item < items; item += p.ncta) {
+      const int b = item / (HKV * splits);
+      const int kvh = (item / splits) % HKV;
+      const int s = item % splits;
+      if (p.q_len[b] == 0) continue;
+      const int kvl = p.kv_len[b];
+      const long long pos = position(p, b);
+      const int chunk = (kvl + splits - 1) / splits;
+      const int j0 = s * chunk, j1 = min(kvl, j0 + chunk);
+      const bf16 *x = p.proj + (size_t)b * p.pstride;
+      // warps 0..G-1: query heads; warp G: new key; warp G+1: new value
+      if (warp <= G) {
+        const bool isk = warp == G;
+        const int hq = kvh * G + warp;
+        const bf16 *src = isk ? x + koff + kvh * D : x + hq * qrow;
+        const bf16 *nw = (const bf16 *)(isk ? w.k_norm : w.q_norm);
+        float v[8], ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < EPL) { v[e] = bf(ldcg_bf(src + lane * EPL + e)); ss = fmaf(v[e], v[e], ss); }
+        ss = warp_sum(ss);
+        const float r = rsqrtf(ss / (float)D + p.eps);
+        float *dst = isk ? kn : qs + warp * D;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < EPL) {
+            const float wv = bf(nw[lane * EPL + e]);
+            v[e] = q35 ? rbf(v[e] * r * (1.f + wv)) : rbf(wv * rbf(v[e] * r));
+            dst[lane * EPL + e] = v[e];
+          }
+        __syncwarp();
+        const int half = RD / 2;
+        const float fpos = (float)pos;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < EPL) {
+            const int d = lane * EPL + e;
+            if (d < RD) {
+              const int fi = d < half ? d : d - half;
+              const float ang = fpos * p.inv_freq[fi];
+              const float cs = rbf(cosf(ang)), sn = rbf(sinf(ang));
+              const float rot = d < half ? -dst[d + half] : dst[d - half];
+              v[e] = rbf(rbf(v[e] * cs) + rbf(rot * sn));
+            }
+          }
+        __syncwarp();
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < EPL) dst[lane * EPL + e] = v[e];
+      } else if (warp == G + 1) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < EPL) vn[lane * EPL + e] = bf(ldcg_bf(x + voff + kvh * D + lane * EPL + e));
+      }
+      csync();
+      bf16 *kc = kc_all + (((size_t)b * HKV + kvh) * p.C) * D;
+      bf16 *vc = vc_all + (((size_t)b * HKV + kvh) * p.C) * D;
+      // KV append (compiler/common/kernels/kv_cache.py:8-42): the s == 0 item writes slot pos.
+      if (s == 0 && pos >= 0 && pos < p.C && tid < D) {
+        kc[(size_t)pos * D + tid] = tobf(kn[tid]);
+        vc[(size_t)pos * D + tid] = tobf(vn[tid]);
+      }
+      // split-KV partial over positions [j0, j1): warp-per-position online softmax
+      float q[4][8], o[4][8], m[4], lsum[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        m[g] = -INFINITY; lsum[g] = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          o[g][e] = 0.f;
+          q[g][e] = (g < G && e < EPL) ? qs[g * D + lane * EPL + e] : 0.f;
+        }
+      }
+      for (int j = j0 + warp; j < j1; j += kWarps) {
+        float kf[8], vf[8];
+        if (j == pos) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (e < EPL) { kf[e] = kn[lane * EPL + e]; vf[e] = vn[lane * EPL + e]; }
+        } else if (EPL == 8) {
+          unpack8(ldnc_u4(kc + (size_t)j * D + lane * 8), kf);
+          unpack8(ldnc_u4(vc + (size_t)j * D + lane * 8), vf);
+        } else {
+          const uint2 ku = ldnc_u2(kc + (size_t)j * D + lane * 4);
+          const uint2 vu = ldnc_u2(vc + (size_t)j * D + lane * 4);
+          kf[0] = bf_lo(ku.x); kf[1] = bf_hi(ku.x); kf[2] = bf_lo(ku.y); kf[3] = bf_hi(ku.y);
+          vf[0] = bf_lo(vu.x); vf[1] = bf_hi(vu.x); vf[2] = bf_lo(vu.y); vf[3] = bf_hi(vu.y);
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          if (g >= G) break;
+          float sc = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (e < EPL) sc = fmaf(q[g][e], kf[e], sc);
+          sc = warp_sum(sc) * scale;
+          const float mn = fmaxf(m[g], sc);
+          const float corr = expf(m[g] - mn);
+          const float pe = expf(sc - mn);
+          lsum[g] = lsum[g] * corr + pe;
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (e < EPL) o[g][e] = fmaf(pe, vf[e], o[g][e] * corr);
+          m[g] = mn;
+        }
+      }
+      // merge the kWarps partial states
+      const int MS = D + 2;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        if (g >= G) break;
+        float *mw = mg + ((size_t)warp * G + g) * MS;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < EPL) mw[lane * EPL + e] = o[g][e];
+        if (lane == 0) { mw[D] = m[g]; mw[D + 1] = lsum[g]; }
+      }
+      csync();
+      for (int idx = tid; idx < G * D; idx += kCT) {
+        const int g = idx / D, d = idx % D;
+        float M = -INFINITY;
+        for (int i = 0; i < kWarps; ++i) M = fmaxf(M, mg[((size_t)i * G + g) * MS + D]);
+        float O = 0.f, Lw = 0.f;
+        if (M != -INFINITY) {
+          for (int i = 0; i < kWarps; ++i) {
+            const float *mw = mg + ((size_t)i * G + g) * MS;
+            const float mi = mw[D];
+            if (mi == -INFINITY) continue;
+            const float f = expf(mi - M);
+            O = fmaf(mw[d], f, O);
+            Lw = fmaf(mw[D + 1], f, Lw);
+          }
+        }
+        const int hq = kvh * G + g;
+        const size_t base = ((size_t)b * HQ + hq) * splits + s;
+        p.att_o[base * D + d] = O;
+        if (d == 0) { p.att_ml[base * 2] = M; p.att_ml[base * 2 + 1] = Lw; }
+      }
+      csync();
+    }
+  }
+
+  // ---- combine split partials, then the Qwen3.5 sigmoid output gate -----------------------
+  __device__ void comb(int) {
+    stage_begin();
+    const int D = p.D, HQ = p.HQ, splits = p.splits;
+    const bool q35 = p.family == XB_FAMILY_QWEN35;
+    const int chunks = D / 32;
+    const int items = p.B * HQ * chunks;
+    float *ms = red;                 // [splits]  (splits <= 256)
+    float *ls = red + 256;           // [splits]
+    float *po = red + 512;           // [kWarps][32] O partials
+    float *pl = red + 512 + 256;     // [kWarps] L partials
+    for (int item = blockIdx.x; item < items; item += p.ncta) {
+      const int b = item / (HQ * chunks);
+      const int hq = (item / chunks) % HQ;
+      const int ck = item % chunks;
+      const int d = ck * 32 + lane;
+      bf16 *dst = p.att_out + (size_t)b * HQ * D + hq * D;
+      if (p.q_len[b] == 0) {
+        if (warp == 0) dst[d] = tobf(0.f);
+        continue;
+      }
+      const size_t base = ((size_t)b * HQ + hq) * splits;
+      for (int s = tid; s < splits; s += kCT) {
+        ms[s] = ldcg_f(p.att_ml + (base + s) * 2);
+        ls[s] = ldcg_f(p.att_ml + (base + s) * 2 + 1);
+      }
+      csync();
+      float M = -INFINITY;
+      for (int s = 0; s < splits; ++s) M = fmaxf(M, ms[s]);
+      float O = 0.f, Lw = 0.f;
+      if (M != -INFINITY)
+        for (int s = warp; s < splits; s += kWarps) {
+          if (ms[s] == -INFINITY) continue;
+          const float f = expf(ms[s] - M);
+          O = fmaf(ldcg_f(p.att_o + (base + s) * D + d), f, O);
+          Lw = fmaf(ls[s], f, Lw);
+        }
+      po[warp * 32 + lane] = O;
+      if (lane == 0) pl[warp] = Lw;
+      csync();
+      if (warp == 0) {
+        float Ot = 0.f, Lt = 0.f;
+        for (int i = 0; i < kWarps; ++i) { Ot += po[i * 32 + lane]; Lt += pl[i]; }
+        float y = Lt > 0.f ? rbf(Ot / Lt) : 0.f;
+        if (q35) {
+          const float gt = bf(ldcg_bf(p.proj + (size_t)b * p.pstride + hq * 2 * D + D + d));
+          const float sg = rbf(1.f / (1.f + expf(-gt)));
+          y = rbf(y * sg);
+        }
+        dst[d] = tobf(y);
+      }
+      csync();
+    }
+  }
+};
+
+template <class V> __device__ void walk_step(const StepParams &p, V &v) {
+  for (int l = 0; l < p.L; ++l) {
+    if (is_delta(p, l)) {
+      v.gemv(l, ST_IN_DELTA);
+      v.delta(l);
+      v.gemv(l, ST_OUT_DELTA);
+    } else {
+      v.gemv(l, ST_QKV);
+      v.attn(l);
+      v.comb(l);
+      v.gemv(l, ST_O);
+    }
+    v.gemv(l, ST_GATEUP);
+    v.gemv(l, ST_DOWN);
+  }
+  v.gemv(-1, ST_LMHEAD);
+}
+
+template <int NB>
+__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ StepParams p) {
+  extern __shared__ __align__(1024) char smem[];
+  SmemHdr *hdr = reinterpret_cast<SmemHdr *>(smem);
+  float *red = reinterpret_cast<float *>(smem + kHdrBytes);
+  char *U = smem + kUOffset;
+  char *ring = U + p.ubytes;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < p.nslots; ++i) {
+      mbar_init(&hdr->full[i], 1);
+      mbar_init(&hdr->empty[i], kWarps);
+    }
+    hdr->abort = 0;
+    hdr->is_last = 0;
+    mbar_fence_init();
+  }
+  // validate token ids once (out-of-range ids are recorded and read as id 0 nowhere: abort)
+  __syncthreads();
+  if (threadIdx.x < p.B) {
+    const long long id = token_id(p, threadIdx.x);
+    if (id < 0 || id >= p.V) atomicCAS(p.ctrl + CTL_ERR, 0u, (unsigned)DERR_TOKEN);
+  }
+  __syncthreads();
+  const bool bad = ld_volatile(p.ctrl + CTL_ERR) != 0;
+  if (threadIdx.x >= kCT) {
+    if (threadIdx.x == kCT && !bad) {
+      Producer pr(p, hdr, ring);
+      walk_step(p, pr);
+      // Drain: never leave with bulk copies in flight into this CTA's shared memory. Phases of
+      // one slot complete in order, so waiting for the last copy issued into each slot suffices.
+      for (int k = max(0, pr.issued - p.nslots); k < pr.issued; ++k) {
+        const int slot = k % p.nslots;
+        const unsigned parity = (unsigned)((k / p.nslots) & 1);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(&hdr->full[slot], parity)) {
+          if (globaltimer() - t0 > kWaitLimitNs) {
+            atomicCAS(p.ctrl + CTL_ERR, 0u, (unsigned)DERR_DRAIN);
+            break;
+          }
+        }
+      }
+    }
+  } else if (!bad) {
+    Consumer<NB> c(p, hdr, red, U, ring);
+    walk_step(p, c);
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------------------------------------
+// Host side
+// ------------------------------------------------------------------------------------------
+thread_local std::string g_err;
+
+int fail(int code, const std::string &msg) {
+  g_err = msg;
+  return code;
+}
+#define XB_CUDA(call)                                                                          \
+  do {                                                                                         \
+    cudaError_t e_ = (call);                                                                   \
+    if (e_ != cudaSuccess)                                                                     \
+      return fail(XB_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));            \
+  } while (0)
+
+} // namespace xb
+
+struct XbModel {
+  XbGeometry g;
+  XbModelWeights w;
+  XbLayerWeights *d_layers = nullptr;  // device table
+  float *d_inv_freq = nullptr;
+  int device = 0;
+  int num_sms = 0;
+};
+
+namespace xb {
+
+struct WsLayout {
+  size_t ctrl, h, proj, core, ssq, att_o, att_ml, att_out, act, am_v, am_i, total;
+  int pstride, max_splits;
+};
+
+static WsLayout ws_layout(const XbGeometry &g, int max_batch, int ncta) {
+  WsLayout L{};
+  const int B = max_batch;
+  const bool q35 = g.family == XB_FAMILY_QWEN35;
+  const int delta_rows = q35 ? (2 * g.lin_key_heads + 2 * g.lin_value_heads) * g.lin_head_dim +
+                                   2 * g.lin_value_heads
+                             : 0;
+  const int attn_rows = g.num_q_heads * g.head_dim * (q35 ? 2 : 1) + 2 * g.num_kv_heads * g.head_dim;
+  L.pstride = ((std::max(delta_rows, attn_rows) + 7) / 8) * 8;
+  L.max_splits = ncta;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t o = off; off += (bytes + 255) & ~size_t(255); return o; };
+  L.ctrl = take(CTL_WORDS * 4);
+  L.h = take((size_t)B * g.hidden * 2);
+  L.proj = take((size_t)B * L.pstride * 2);
+  const int vdim = q35 ? g.lin_value_heads * g.lin_head_dim : 8;
+  L.core = take((size_t)B * vdim * 2);
+  L.ssq = take((size_t)B * (q35 ? g.lin_value_heads : 1) * 8 * 4);
+  L.att_o = take((size_t)B * g.num_q_heads * L.max_splits * g.head_dim * 4);
+  L.att_ml = take((size_t)B * g.num_q_heads * L.max_splits * 2 * 4);
+  L.att_out = take((size_t)B * g.num_q_heads * g.head_dim * 2);
+  L.act = take((size_t)B * g.intermediate * 2);
+  L.am_v = take((size_t)ncta * XB_MAX_BATCH * 4);
+  L.am_i = take((size_t)ncta * XB_MAX_BATCH * 4);
+  L.total = off;
+  return L;
+}
+
+static int check_geometry(const XbGeometry &g) {
+  const bool q35 = g.family == XB_FAMILY_QWEN35;
+  if (g.family != XB_FAMILY_QWEN3 && !q35) return fail(XB_ERR_INVALID, "unknown model family");
+  if (g.num_layers < 1 || g.num_layers > XB_MAX_LAYERS)
+    return fail(XB_ERR_INVALID, "num_layers must be 1..64");
+  if (g.hidden % 256 || g.intermediate % 8 || g.vocab < 1)
+    return fail(XB_ERR_INVALID, "hidden must be a multiple of 256, intermediate of 8");
+  if (g.num_kv_heads < 1 || g.num_q_heads % g.num_kv_heads)
+    return fail(XB_ERR_INVALID, "query heads must be a positive multiple of KV heads");
+  const int G = g.num_q_heads / g.num_kv_heads;
+  if (G > 4) return fail(XB_ERR_UNSUPPORTED, "at most 4 query heads per KV head");
+  if (g.head_dim != 128 && g.head_dim != 256)
+    return fail(XB_ERR_UNSUPPORTED, "head_dim must be 128 or 256");
+  if (g.rotary_dim < 2 || g.rotary_dim > g.head_dim || g.rotary_dim % 2)
+    return fail(XB_ERR_INVALID, "invalid rotary_dim");
+  if (g.capacity < 1) return fail(XB_ERR_INVALID, "capacity must be positive");
+  if (g.state_rows < 1 || g.state_rows > XB_MAX_BATCH)
+    return fail(XB_ERR_INVALID, "state_rows must be 1..8");
+  for (int l = 0; l < g.num_layers; ++l) {
+    const int k = g.layer_kind[l];
+    if (k != XB_LAYER_ATTENTION && k != XB_LAYER_DELTANET)
+      return fail(XB_ERR_INVALID, "invalid layer kind");
+    if (k == XB_LAYER_DELTANET && !q35)
+      return fail(XB_ERR_INVALID, "DeltaNet layers need the Qwen3.5 family");
+  }
+  if (q35) {
+    if (g.lin_head_dim != 128 || g.lin_key_heads < 1 || g.lin_value_heads % g.lin_key_heads ||
+        g.conv_width != 4)
+      return fail(XB_ERR_UNSUPPORTED, "DeltaNet needs key/value dim 128, width-4 conv");
+    if (g.lin_value_heads * g.lin_head_dim > 8192 || 2 * g.lin_head_dim > kCT)
+      return fail(XB_ERR_UNSUPPORTED, "DeltaNet value width too large");
+  }
+  // every GEMV must fit at least one row (two for gate/up) into a 32 KB ring slot
+  const int kmax = std::max(g.intermediate, std::max(g.hidden, g.num_q_heads * g.head_dim));
+  if (kmax * 2 > kSlot || g.hidden * 4 > kSlot)
+    return fail(XB_ERR_UNSUPPORTED, "GEMV input dimension too large for a ring slot");
+  return XB_OK;
+}
+
+static size_t ubytes_for(const XbGeometry &g, int NB) {
+  const bool q35 = g.family == XB_FAMILY_QWEN35;
+  int kmax = std::max(g.hidden, g.intermediate);
+  kmax = std::max(kmax, g.num_q_heads * g.head_dim);
+  if (q35) kmax = std::max(kmax, g.lin_value_heads * g.lin_head_dim);
+  const size_t act = (size_t)NB * kmax * 2;
+  const int G = g.num_q_heads / g.num_kv_heads;
+  const size_t att = ((size_t)G * g.head_dim + 2 * g.head_dim + (size_t)kWarps * G * (g.head_dim + 2)) * 4;
+  const size_t u = std::max(act, att);
+  return (u + 127) & ~size_t(127);
+}
+
+template <int NB> static int configure_kernel(size_t smem) {
+  // The attribute is per function and process-wide; set it once to the largest size used.
+  static std::mutex mu;
+  static size_t configured = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (smem <= configured) return XB_OK;
+  XB_CUDA(cudaFuncSetAttribute(decode_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)kSmemLimit));
+  configured = kSmemLimit;
+  return XB_OK;
+}
+
+template <int NB>
+static int launch(const StepParams &prm, size_t smem, int ncta, cudaStream_t stream) {
+  int rc = configure_kernel<NB>(smem);
+  if (rc) return rc;
+  void *args[] = {const_cast<StepParams *>(&prm)};
+  XB_CUDA(cudaLaunchCooperativeKernel((const void *)decode_kernel<NB>, dim3(ncta), dim3(kThreads),
+                                      args, smem, stream));
+  return XB_OK;
+}
+
+} // namespace xb
+
+using namespace xb;
+
+extern "C" {
+
+const char *xb_last_error(void) { return g_err.c_str(); }
+int xb_abi_version(void) { return XB_ABI_VERSION; }
+
+int xb_rope_inv_freq(float theta, int32_t rotary_dim, float *out) {
+  if (!out || rotary_dim < 2 || rotary_dim % 2 || !(theta > 0.f))
+    return fail(XB_ERR_INVALID, "invalid RoPE parameters");
+  for (int i = 0; i < rotary_dim / 2; ++i) {
+    const float expo = (float)(2 * i) / (float)rotary_dim;
+    out[i] = 1.0f / powf(theta, expo);
+  }
+  return XB_OK;
+}
+
+int xb_model_create(const XbGeometry *geometry, const XbModelWeights *weights, XbModel **model) {
+  if (!geometry || !weights || !model) return fail(XB_ERR_INVALID, "null argument");
+  *model = nullptr;
+  int rc = check_geometry(*geometry);
+  if (rc) return rc;
+  const XbGeometry &g = *geometry;
+  auto aligned = [](const void *ptr) { return ((uintptr_t)ptr & 15) == 0; };
+  if (!weights->embed || !weights->final_norm || !weights->lm_head)
+    return fail(XB_ERR_INVALID, "embed, final_norm and lm_head are required");
+  if (!aligned(weights->lm_head)) return fail(XB_ERR_INVALID, "lm_head must be 16-byte aligned");
+  for (int l = 0; l < g.num_layers; ++l) {
+    const XbLayerWeights &w = weights->layers[l];
+    std::vector<const void *> need = {w.input_norm, w.post_norm, w.gate, w.up, w.down};
+    std::vector<const void *> streamed = {w.gate, w.up, w.down};
+    if (g.layer_kind[l] == XB_LAYER_DELTANET) {
+      for (auto q : {w.in_qkv, w.in_z, w.in_b, w.in_a, w.conv_w, w.a_log, w.dt_bias, w.gnorm,
+                     w.out_proj})
+        need.push_back(q);
+      for (auto q : {w.in_qkv, w.in_z, w.in_b, w.in_a, w.out_proj}) streamed.push_back(q);
+    } else {
+      for (auto q : {w.q_proj, w.k_proj, w.v_proj, w.o_proj, w.q_norm, w.k_norm}) need.push_back(q);
+      for (auto q : {w.q_proj, w.k_proj, w.v_proj, w.o_proj}) streamed.push_back(q);
+    }
+    for (auto q : need)
+      if (!q) return fail(XB_ERR_INVALID, "missing weight pointer in layer " + std::to_string(l));
+    for (auto q : streamed)
+      if (!aligned(q))
+        return fail(XB_ERR_INVALID, "projection weights must be 16-byte aligned (layer " +
+                                        std::to_string(l) + ")");
+  }
+  XbModel *m = new XbModel();
+  m->g = g;
+  m->w = *weights;
+  cudaGetDevice(&m->device);
+  cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, m->device);
+  if (cudaMalloc(&m->d_layers, sizeof(XbLayerWeights) * g.num_layers) != cudaSuccess ||
+      cudaMalloc(&m->d_inv_freq, sizeof(float) * (g.rotary_dim / 2)) != cudaSuccess) {
+    cudaFree(m->d_layers);
+    delete m;
+    return fail(XB_ERR_CUDA, "cudaMalloc failed for the model plan");
+  }
+  // RoPE inverse frequencies as the HF default rope init: 1 / theta^(2i / dim), fp32.
+  std::vector<float> inv(g.rotary_dim / 2);
+  if (g.rope_inv_freq) {
+    memcpy(inv.data(), g.rope_inv_freq, sizeof(float) * inv.size());
+  } else {
+    xb_rope_inv_freq(g.rope_theta, g.rotary_dim, inv.data());
+  }
+  cudaMemcpy(m->d_layers, weights->layers, sizeof(XbLayerWeights) * g.num_layers,
+             cudaMemcpyHostToDevice);
+  cudaMemcpy(m->d_inv_freq, inv.data(), sizeof(float) * inv.size(), cudaMemcpyHostToDevice);
+  *model = m;
+  return XB_OK;
+}
+
+int xb_model_destroy(XbModel *model) {
+  if (!model) return XB_OK;
+  cudaFree(model->d_layers);
+  cudaFree(model->d_inv_freq);
+  delete model;
+  return XB_OK;
+}
+
+int xb_decode_workspace_bytes(const XbModel *model, int32_t max_batch, size_t *bytes) {
+  if (!model || !bytes) return fail(XB_ERR_INVALID, "null argument");
+  if (max_batch < 1 || max_batch > XB_MAX_BATCH) return fail(XB_ERR_INVALID, "max_batch 1..8");
+  *bytes = ws_layout(model->g, max_batch, model->num_sms).total;
+  return XB_OK;
+}
+
+int xb_workspace_init(void *workspace, size_t workspace_bytes, void *stream) {
+  if (!workspace) return fail(XB_ERR_INVALID, "null workspace");
+  XB_CUDA(cudaMemsetAsync(workspace, 0, workspace_bytes, (cudaStream_t)stream));
+  return XB_OK;
+}
+
+int xb_workspace_check(void *workspace, void *stream, int32_t *device_error) {
+  if (!workspace) return fail(XB_ERR_INVALID, "null workspace");
+  unsigned err = 0;
+  XB_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  XB_CUDA(cudaMemcpy(&err, (unsigned *)workspace + CTL_ERR, 4, cudaMemcpyDeviceToHost));
+  if (device_error) *device_error = (int32_t)err;
+  if (err) {
+    // reset the control words so the workspace can be reused
+    XB_CUDA(cudaMemset(workspace, 0, CTL_WORDS * 4));
+    return fail(XB_ERR_DEVICE, "device-side error code " + std::to_string(err));
+  }
+  return XB_OK;
+}
+
+int xb_decode_step(const XbModel *model, const XbStepArgs *args, void *workspace,
+                   size_t workspace_bytes, void *stream) {
+  if (!model || !args || !workspace) return fail(XB_ERR_INVALID, "null argument");
+  const XbGeometry &g = model->g;
+  const int B = args->batch;
+  if (B < 1 || B > XB_MAX_BATCH || B > g.state_rows)
+    return fail(XB_ERR_INVALID, "batch must be 1..min(8, state_rows)");
+  if (!args->logits) return fail(XB_ERR_INVALID, "logits are required");
+  if (!args->input_ids != !args->cache_position)
+    return fail(XB_ERR_INVALID, "pass both input_ids and cache_position on the device, or neither");
+  int active = 0, max_kv = 1;
+  for (int b = 0; b < B; ++b) {
+    const int q = args->query_lengths[b], kv = args->kv_lengths[b];
+    if (q != 0 && q != 1) return fail(XB_ERR_INVALID, "decode query lengths must be 0 or 1");
+    if (kv < q || kv < 1 || kv > g.capacity) return fail(XB_ERR_INVALID, "Invalid query/KV lengths");
+    active += q;
+    max_kv = std::max(max_kv, kv);
+  }
+  if (!active) return fail(XB_ERR_INVALID, "at least one row must be active");
+  for (int l = 0; l < g.num_layers; ++l) {
+    const XbLayerState &s = args->layers[l];
+    if (g.layer_kind[l] == XB_LAYER_DELTANET) {
+      if (!s.conv_in || !s.rec_in || !s.conv_out || !s.rec_out)
+        return fail(XB_ERR_INVALID, "missing DeltaNet state in layer " + std::to_string(l));
+      // conv_out / rec_out either equal their input (update in place) or do not overlap it.
+    } else if (!s.k_cache || !s.v_cache) {
+      return fail(XB_ERR_INVALID, "missing KV cache in layer " + std::to_string(l));
+    }
+  }
+  const int ncta = model->num_sms;
+  const WsLayout Lb = ws_layout(g, B, ncta);
+  if (workspace_bytes < Lb.total) return fail(XB_ERR_INVALID, "workspace too small");
+  if (((uintptr_t)workspace & 255) != 0) return fail(XB_ERR_INVALID, "workspace must be 256-byte aligned");
+
+  StepParams p;
+  memset(&p, 0, sizeof(p));
+  const bool q35 = g.family == XB_FAMILY_QWEN35;
+  p.family = g.family; p.L = g.num_layers; p.H = g.hidden; p.I = g.intermediate; p.V = g.vocab;
+  p.HQ = g.num_q_heads; p.HKV = g.num_kv_heads; p.D = g.head_dim; p.RD = g.rotary_dim;
+  p.HK = q35 ? g.lin_key_heads : 1; p.HV = q35 ? g.lin_value_heads : 1;
+  p.DK = q35 ? g.lin_head_dim : 128; p.CW = q35 ? g.conv_width : 4; p.C = g.capacity;
+  p.rows_alloc = g.state_rows; p.eps = g.rms_eps;
+  // (float)(d ** -0.5) as the reference's Python constants: recurrent.py:23, attention scaling.
+  p.dk_scale = (float)(1.0 / std::sqrt((double)p.DK));
+  p.att_scale = (float)(1.0 / std::sqrt((double)g.head_dim));
+  p.pstride = Lb.pstride;
+  // split-KV: enough (row, kv head, split) items to cover every SM, >= 16 positions per split
+  int splits = std::max(1, ncta / std::max(1, active * g.num_kv_heads));
+  splits = std::min(splits, std::max(1, (max_kv + 15) / 16));
+  splits = std::min(splits, std::min(Lb.max_splits, 256));
+  p.splits = splits;
+  p.ncta = ncta;
+  p.B = B;
+  for (int b = 0; b < B; ++b) { p.kv_len[b] = args->kv_lengths[b]; p.q_len[b] = args->query_lengths[b]; }
+  p.delta_mask = 0;
+  for (int l = 0; l < g.num_layers; ++l)
+    if (g.layer_kind[l] == XB_LAYER_DELTANET) p.delta_mask |= 1ull << l;
+  p.layers = model->d_layers;
+  p.embed = (const bf16 *)model->w.embed;
+  p.final_norm = (const bf16 *)model->w.final_norm;
+  p.lm_head = (const bf16 *)model->w.lm_head;
+  p.inv_freq = model->d_inv_freq;
+  p.ids = args->input_ids;
+  p.pos = args->cache_position;
+  for (int b = 0; b < B; ++b) {
+    p.hid[b] = args->host_ids[b];
+    p.hpos[b] = args->host_positions[b];
+    if (!p.ids && (args->host_ids[b] < 0 || args->host_ids[b] >= g.vocab))
+      return fail(XB_ERR_INVALID, "token id out of range");
+  }
+  for (int l = 0; l < g.num_layers; ++l) {
+    const XbLayerState &s = args->layers[l];
+    if (g.layer_kind[l] == XB_LAYER_DELTANET) {
+      p.sa[l] = const_cast<void *>(s.conv_in);
+      p.sb[l] = const_cast<void *>(s.rec_in);
+      p.sc[l] = s.conv_out;
+      p.sd[l] = s.rec_out;
+    } else {
+      p.sa[l] = s.k_cache;
+      p.sb[l] = s.v_cache;
+    }
+  }
+  p.logits = (bf16 *)args->logits;
+  p.tokens = args->next_tokens;
+  char *ws = (char *)workspace;
+  p.ctrl = (unsigned *)(ws + Lb.ctrl);
+  p.h = (bf16 *)(ws + Lb.h);
+  p.proj = (bf16 *)(ws + Lb.proj);
+  p.core = (bf16 *)(ws + Lb.core);
+  p.ssq = (float *)(ws + Lb.ssq);
+  p.att_o = (float *)(ws + Lb.att_o);
+  p.att_ml = (float *)(ws + Lb.att_ml);
+  p.att_out = (bf16 *)(ws + Lb.att_out);
+  p.act = (bf16 *)(ws + Lb.act);
+  p.am_v = (float *)(ws + Lb.am_v);
+  p.am_i = (int *)(ws + Lb.am_i);
+
+  const int NB = B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : 8;
+  p.ubytes = (int)ubytes_for(g, NB);
+  const size_t fixed = kUOffset + (size_t)p.ubytes;
+  int nslots = (int)((kSmemLimit - fixed) / kSlot);
+  nslots = std::min(nslots, kMaxSlots);
+  if (nslots < 2) return fail(XB_ERR_UNSUPPORTED, "not enough shared memory for the weight ring");
+  p.nslots = nslots;
+  const size_t smem = fixed + (size_t)nslots * kSlot;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (NB) {
+  case 1: return launch<1>(p, smem, ncta, st);
+  case 2: return launch<2>(p, smem, ncta, st);
+  case 4: return launch<4>(p, smem, ncta, st);
+  default: return launch<8>(p, smem, ncta, st);
+  }
+}
+
+} // extern "C"
