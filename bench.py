@@ -49,6 +49,7 @@ def parse():
     ap.add_argument("--capacity", type=int, default=4096)
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--trace", help="save a per-CTA stage trace of one extra step to this file")
     return ap.parse_args()
 
 
@@ -321,6 +322,17 @@ def main():
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
     }
+    if args.trace and rank == 0:
+        from xinfer_b200 import _native as nat
+
+        buf = torch.zeros(nat.TRACE_BYTES // 8, dtype=torch.int64, device=dev)
+        nat.check(nat.load().xb_debug_trace(buf.data_ptr(), nat.TRACE_BYTES))
+        runner.reset()
+        runner.prefill(prompt[:64])
+        torch.cuda.synchronize(dev)
+        nat.check(nat.load().xb_debug_trace(None, 0))
+        torch.save({"trace": buf.cpu(), "ncta": torch.cuda.get_device_properties(dev).multi_processor_count,
+                    "stride": nat.TRACE_STRIDE, "stages": nat.TRACE_STAGES}, args.trace)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args, g, args.cpu_seconds)
     eng.close()

@@ -135,6 +135,13 @@ int xb_workspace_check(void *workspace, void *stream, int32_t *device_error);
  * compiler/qwen35/model.py:41 and compiler/qwen3/model.py:16-26). */
 int xb_rope_inv_freq(float theta, int32_t rotary_dim, float *out);
 
+/* Stage trace for performance work (the reference has no in-process tracer; it profiles with
+ * external tools). While a device buffer is set, every xb_decode_step launch writes, per CTA,
+ * (2 * 512 + 4) u64 words: %globaltimer at each stage's barrier arrival and release, the
+ * kernel end time, the consumers' total ring-slot wait, the stage count and the producer's
+ * busy time. Pass NULL to switch tracing off. The buffer must hold 1024 CTAs' worth. */
+int xb_debug_trace(void *device_buffer, size_t bytes);
+
 const char *xb_last_error(void);
 int xb_abi_version(void);
 

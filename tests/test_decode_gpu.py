@@ -22,6 +22,9 @@ pytestmark = pytest.mark.gpu
 LOGIT_MAX_ABS = 2e-2
 LOGIT_COS = 0.9999
 STATE_REL = 1e-2
+# full-depth random-init models sit at a measured bf16 noise floor (see tests/test_oracle.py)
+FULL_MAX_ABS = 0.15
+FULL_COS = 0.999
 GOLDEN = Path(__file__).resolve().parent / "golden"
 
 _MODELS = {}
@@ -54,10 +57,14 @@ class LazyWeights(dict):
 
 
 def check_logits(got, want, where):
+    """North-star bar per element: |got - want| <= 2e-2, widened by one bf16 ulp of the
+    reference value (2^-7 |want|) because bf16 logits above 2.56 have an ulp larger than 2e-2;
+    plus cosine >= 0.9999 over the row."""
     got, want = got.float().cpu(), want.float().cpu()
+    excess = ((got - want).abs() - (LOGIT_MAX_ABS + want.abs() * 2.0 ** -7)).max().item()
     err = (got - want).abs().max().item()
     cos = O.cosine(got, want)
-    assert err <= LOGIT_MAX_ABS and cos >= LOGIT_COS, f"{where}: max abs {err}, cosine {cos}"
+    assert excess <= 0 and cos >= LOGIT_COS, f"{where}: max abs {err}, cosine {cos}"
 
 
 def run_schedule_gpu(eng, g, schedule, device, rows_alloc=8):
@@ -133,6 +140,24 @@ def test_single_row_matches_oracle(name, cuda_device):
             n = len(sched)
             assert O.rel_l2(a[:, :, :n], b[:, :, :n]) <= STATE_REL, f"kv {i}"
             assert torch.count_nonzero(a[:, :, n:]) == 0, "KV written outside the appended slots"
+
+
+@pytest.mark.parametrize("name", ["qwen3-0.6b-l2", "qwen3.5-0.8b-l4", "qwen3.5-4b-l4"])
+def test_full_width_matches_oracle(name, cuda_device):
+    """Real hidden size, heads and 150K/248K vocabulary; shallow stack, tight bar."""
+    g, sd, W, eng = model(name, 64, cuda_device, jitter=0.1)
+    sched = schedule_single(g, 6, seed=8)
+    got, toks, state, _ = run_schedule_gpu(eng, g, sched, cuda_device)
+    want, ostate = run_schedule_oracle(g, W, sched, 64)
+    for s in range(len(sched)):
+        check_logits(got[s, 0], want[s, 0], f"{name} step {s}")
+        assert int(toks[s, 0]) == int(torch.argmax(got[s, 0].float()))
+    for i, (a, b) in enumerate(zip(state, ostate)):
+        n = len(sched)
+        a, b = a.float().cpu(), b.float()
+        if not g.is_delta(i // 2):
+            a, b = a[:, :, :n], b[:, :, :n]
+        assert O.rel_l2(a, b) <= STATE_REL, f"state {i}"
 
 
 @pytest.mark.parametrize("name", ["qwen3-tiny", "qwen3.5-tiny"])
@@ -253,11 +278,12 @@ def test_matches_reference_fixtures(fixture, cuda_device):
                 idx = summary["top_indices"][s, r]
                 vals = got[s, r].float().cpu()[idx]
                 err = (vals - summary["top_values"][s, r].float()).abs().max().item()
-                assert err <= LOGIT_MAX_ABS, f"{fixture} step {s}: top-32 logits differ by {err}"
+                assert err <= FULL_MAX_ABS, f"{fixture} step {s}: top-32 logits differ by {err}"
                 sl = got[s, r, ::97].float().cpu()
                 ref = summary["stride_slice"][s, r].float()
-                assert O.cosine(sl, ref) >= LOGIT_COS
-                assert (sl - ref).abs().max().item() <= LOGIT_MAX_ABS
+                assert O.cosine(sl, ref) >= FULL_COS
+                assert (sl - ref).abs().max().item() <= FULL_MAX_ABS
+    rel = STATE_REL if fx["logits"] is not None else 5 * STATE_REL
     for i, smp in enumerate(fx["state_sample"]):
         a = state[i].reshape(-1)[smp["index"].long().to(cuda_device)].float().cpu()
-        assert O.rel_l2(a, smp["value"].float()) <= STATE_REL, f"{fixture} state {i}"
+        assert O.rel_l2(a, smp["value"].float()) <= rel, f"{fixture} state {i}"

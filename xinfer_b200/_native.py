@@ -22,8 +22,11 @@ LIBRARY_PATH = Path(__file__).resolve().parent / LIBRARY_NAME
 EXPORTED = (
     "xb_model_create", "xb_model_destroy", "xb_decode_workspace_bytes", "xb_workspace_init",
     "xb_decode_step", "xb_workspace_check", "xb_rope_inv_freq", "xb_last_error",
-    "xb_abi_version",
+    "xb_abi_version", "xb_debug_trace",
 )
+TRACE_STAGES = 512
+TRACE_STRIDE = 2 * TRACE_STAGES + 4
+TRACE_BYTES = TRACE_STRIDE * 8 * 1024
 
 vp = ctypes.c_void_p
 
@@ -116,6 +119,7 @@ def load():
         "xb_decode_step": (i32, [vp, ctypes.POINTER(XbStepArgs), vp, sz, vp]),
         "xb_workspace_check": (i32, [vp, vp, ctypes.POINTER(i32)]),
         "xb_rope_inv_freq": (i32, [ctypes.c_float, i32, ctypes.POINTER(ctypes.c_float)]),
+        "xb_debug_trace": (i32, [vp, sz]),
         "xb_last_error": (ctypes.c_char_p, []),
         "xb_abi_version": (i32, []),
     }

@@ -95,9 +95,17 @@ QWEN35_TINY_HV32 = replace(
     layer_types=(),
 )
 
+# Full-width, reduced-depth variants: every kernel runs at its real dimensions (hidden, heads,
+# vocabulary) while the shallow stack keeps one-ulp rounding flips from cascading, so parity can
+# be held to the tight bar at full width.
+QWEN3_0_6B_L2 = replace(QWEN3_0_6B, name="qwen3-0.6b-l2", num_layers=2, layer_types=())
+QWEN35_0_8B_L4 = replace(QWEN35_0_8B, name="qwen3.5-0.8b-l4", num_layers=4, layer_types=())
+QWEN35_4B_L4 = replace(QWEN35_4B, name="qwen3.5-4b-l4", num_layers=4, layer_types=())
+
 CONFIGS = {
     g.name: g
-    for g in (QWEN3_0_6B, QWEN35_0_8B, QWEN35_4B, QWEN3_TINY, QWEN35_TINY, QWEN35_TINY_HV32)
+    for g in (QWEN3_0_6B, QWEN35_0_8B, QWEN35_4B, QWEN3_TINY, QWEN35_TINY, QWEN35_TINY_HV32,
+              QWEN3_0_6B_L2, QWEN35_0_8B_L4, QWEN35_4B_L4)
 }
 
 

@@ -71,7 +71,12 @@ struct StepParams {
   bf16 *h, *proj, *core, *att_out, *act;
   float *ssq, *att_o, *att_ml, *am_v;
   int *am_i;
+  // Optional stage trace (see xb_debug_trace): per CTA kTraceStages x {arrive, release} stamps
+  // of %globaltimer plus ring-wait totals; NULL when tracing is off.
+  unsigned long long *trace;
 };
+constexpr int kTraceStages = 512;
+constexpr int kTraceStride = 2 * kTraceStages + 4;  // u64 words per CTA
 
 struct SmemHdr {
   uint64_t full[kMaxSlots];
@@ -252,6 +257,8 @@ template <int NB> struct Consumer {
   unsigned phase = 0;
   bool first = true;      // first stage of the step needs no barrier
   bool h_ready = false;   // residual stream in p.h (false: still the embedding rows)
+  int sidx = 0;           // stage counter (trace)
+  unsigned long long full_wait = 0;  // ns spent waiting for ring slots (trace, tid 0)
   // running argmax for the lm_head stage (lane b keeps batch row b)
   float am_v = -INFINITY;
   int am_i = 0x7fffffff;
@@ -306,14 +313,33 @@ template <int NB> struct Consumer {
   }
 
   __device__ void stage_begin() {
-    if (first) { first = false; return; }
-    grid_sync();
+    unsigned long long *tr = p.trace ? p.trace + (size_t)blockIdx.x * kTraceStride : nullptr;
+    const int si = sidx < kTraceStages ? sidx : kTraceStages - 1;
+    if (tr && tid == 0) tr[2 * si] = globaltimer();
+    if (first) first = false;
+    else grid_sync();
+    if (tr && tid == 0) tr[2 * si + 1] = globaltimer();
+    ++sidx;
+  }
+  __device__ void trace_end() {
+    if (p.trace && tid == 0) {
+      unsigned long long *tr = p.trace + (size_t)blockIdx.x * kTraceStride;
+      tr[2 * kTraceStages] = globaltimer();
+      tr[2 * kTraceStages + 1] = full_wait;
+      tr[2 * kTraceStages + 2] = (unsigned long long)sidx;
+    }
   }
 
   __device__ const char *wait_full() {
     if (aborted()) return nullptr;
     uint64_t t0 = 0;
     unsigned spins = 0;
+    if (p.trace && tid == 0 && !mbar_try_wait(&hdr->full[slot], phase)) {
+      const uint64_t a = globaltimer();
+      while (!mbar_try_wait(&hdr->full[slot], phase) && globaltimer() - a < kWaitLimitNs) {
+      }
+      full_wait += globaltimer() - a;
+    }
     while (!mbar_try_wait(&hdr->full[slot], phase)) {
       if ((++spins & 63u) == 0) {
         if (aborted()) return nullptr;
@@ -970,7 +996,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   if (threadIdx.x >= kCT) {
     if (threadIdx.x == kCT && !bad) {
       Producer pr(p, hdr, ring);
+      const uint64_t t_start = globaltimer();
       walk_step(p, pr);
+      if (p.trace) p.trace[(size_t)blockIdx.x * kTraceStride + 2 * kTraceStages + 3] = globaltimer() - t_start;
       // Drain: never leave with bulk copies in flight into this CTA's shared memory. Phases of
       // one slot complete in order, so waiting for the last copy issued into each slot suffices.
       for (int k = max(0, pr.issued - p.nslots); k < pr.issued; ++k) {
@@ -988,6 +1016,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   } else if (!bad) {
     Consumer<NB> c(p, hdr, red, U, ring);
     walk_step(p, c);
+    c.trace_end();
   }
   __syncthreads();
 }
@@ -996,6 +1025,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
 // Host side
 // ------------------------------------------------------------------------------------------
 thread_local std::string g_err;
+static unsigned long long *g_trace = nullptr;  // xb_debug_trace
 
 int fail(int code, const std::string &msg) {
   g_err = msg;
@@ -1135,6 +1165,14 @@ extern "C" {
 
 const char *xb_last_error(void) { return g_err.c_str(); }
 int xb_abi_version(void) { return XB_ABI_VERSION; }
+
+int xb_debug_trace(void *device_buffer, size_t bytes) {
+  const size_t need = (size_t)kTraceStride * 8 * 1024;
+  if (device_buffer && bytes < need)
+    return fail(XB_ERR_INVALID, "trace buffer needs " + std::to_string(need) + " bytes");
+  g_trace = static_cast<unsigned long long *>(device_buffer);
+  return XB_OK;
+}
 
 int xb_rope_inv_freq(float theta, int32_t rotary_dim, float *out) {
   if (!out || rotary_dim < 2 || rotary_dim % 2 || !(theta > 0.f))
@@ -1332,6 +1370,7 @@ int xb_decode_step(const XbModel *model, const XbStepArgs *args, void *workspace
   p.act = (bf16 *)(ws + Lb.act);
   p.am_v = (float *)(ws + Lb.am_v);
   p.am_i = (int *)(ws + Lb.am_i);
+  p.trace = g_trace;
 
   const int NB = B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : 8;
   p.ubytes = (int)ubytes_for(g, NB);
