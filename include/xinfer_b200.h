@@ -130,6 +130,24 @@ int xb_decode_step(const XbModel *model, const XbStepArgs *args, void *workspace
  * device-side error since the last call (and clears it). */
 int xb_workspace_check(void *workspace, void *stream, int32_t *device_error);
 
+/* Allocation-free decode step. No counterpart in the reference: this entry point exists for
+ * callers that cannot allocate device memory when they step the model (a serving runtime that
+ * reserved HBM for its own pool at start-up, work issued while a stream is being captured, a
+ * host with a fixed memory plan). It takes the geometry and weight pointers directly (no
+ * XbModel, whose creation allocates) and no workspace: the weight table, RoPE table and the
+ * kernel's scratch live in one static device array of XB_STATIC_SCRATCH_BYTES, held by every
+ * GPU that loads this library until the process exits. Steps whose scratch would not fit
+ * (large batch or many heads) fail with XB_ERR_INVALID and a message; use xb_decode_step.
+ * It calls no cudaMalloc / cudaFree. The first call on each device does a one-time set-up
+ * (a symbol address lookup, no allocation); make that first call before any stream capture.
+ * All calls on a device share the array, which keeps the previous call's contents: each call
+ * rewrites the tables and clears the control words, so calls that overlap on the GPU (other
+ * streams, other threads) race and must be serialised by the caller. If device_error is not
+ * NULL the call synchronises the stream and reports the kernel's device-side error word. */
+#define XB_STATIC_SCRATCH_BYTES (4u << 20)
+int xb_decode_step_static(const XbGeometry *geometry, const XbModelWeights *weights,
+                          const XbStepArgs *args, void *stream, int32_t *device_error);
+
 /* Host-only helper: the HF default RoPE inverse frequencies 1 / theta^(2i / rotary_dim) in fp32
  * (transformers Qwen3_5TextRotaryEmbedding.compute_default_rope_parameters, as loaded by
  * compiler/qwen35/model.py:41 and compiler/qwen3/model.py:16-26). */

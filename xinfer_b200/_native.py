@@ -22,11 +22,12 @@ LIBRARY_PATH = Path(__file__).resolve().parent / LIBRARY_NAME
 EXPORTED = (
     "xb_model_create", "xb_model_destroy", "xb_decode_workspace_bytes", "xb_workspace_init",
     "xb_decode_step", "xb_workspace_check", "xb_rope_inv_freq", "xb_last_error",
-    "xb_abi_version", "xb_debug_trace",
+    "xb_abi_version", "xb_decode_step_static", "xb_debug_trace",
 )
 TRACE_STAGES = 512
 TRACE_STRIDE = 2 * TRACE_STAGES + 4
 TRACE_BYTES = TRACE_STRIDE * 8 * 1024
+STATIC_SCRATCH_BYTES = 4 << 20
 
 vp = ctypes.c_void_p
 
@@ -119,6 +120,8 @@ def load():
         "xb_decode_step": (i32, [vp, ctypes.POINTER(XbStepArgs), vp, sz, vp]),
         "xb_workspace_check": (i32, [vp, vp, ctypes.POINTER(i32)]),
         "xb_rope_inv_freq": (i32, [ctypes.c_float, i32, ctypes.POINTER(ctypes.c_float)]),
+        "xb_decode_step_static": (i32, [ctypes.POINTER(XbGeometry), ctypes.POINTER(XbModelWeights),
+                                        ctypes.POINTER(XbStepArgs), vp, ctypes.POINTER(i32)]),
         "xb_debug_trace": (i32, [vp, sz]),
         "xb_last_error": (ctypes.c_char_p, []),
         "xb_abi_version": (i32, []),

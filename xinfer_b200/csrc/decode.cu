@@ -1390,3 +1390,129 @@ int xb_decode_step(const XbModel *model, const XbStepArgs *args, void *workspace
 }
 
 } // extern "C"
+
+// ------------------------------------------------------------------------------------------
+// Allocation-free variant of xb_decode_step.
+//
+// Some callers cannot allocate device memory at the moment they run a decode step: serving
+// stacks that reserve (nearly) all of HBM for their own pool at start-up, so a later cudaMalloc
+// fails or fragments that pool; code that runs while a stream is being captured, where a
+// cudaMalloc would not be part of the captured work; and hosts with a fixed memory plan that
+// forbids allocations after initialisation. This entry point needs neither an XbModel (whose
+// creation allocates the weight table) nor a caller workspace: the per-layer weight table, the
+// RoPE table and the kernel's scratch all live in one file-scope device array of
+// XB_STATIC_SCRATCH_BYTES, which every GPU that loads this library keeps until the process exits.
+// ------------------------------------------------------------------------------------------
+namespace xb {
+
+constexpr size_t kStaticScratchBytes = XB_STATIC_SCRATCH_BYTES;
+constexpr size_t kStaticTableBytes = sizeof(XbLayerWeights) * XB_MAX_LAYERS;   // weight table
+constexpr size_t kStaticRopeBytes = 4096;                                      // inv_freq floats
+constexpr size_t kStaticWsOffset = ((kStaticTableBytes + kStaticRopeBytes) + 255) & ~size_t(255);
+constexpr int kStaticMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+struct StaticDevice {
+  bool ready = false;
+  unsigned char *base = nullptr;  // device address of g_static_scratch on this device
+  int num_sms = 0;
+};
+
+} // namespace xb
+
+extern "C" int xb_decode_step_static(const XbGeometry *geometry, const XbModelWeights *weights,
+                                     const XbStepArgs *args, void *stream,
+                                     int32_t *device_error) {
+  using namespace xb;
+  static std::mutex mu;
+  static StaticDevice devices[kStaticMaxDevices];
+  if (!geometry || !weights || !args) return fail(XB_ERR_INVALID, "null argument");
+  int rc = check_geometry(*geometry);
+  if (rc) return rc;
+  const XbGeometry &g = *geometry;
+  const int B = args->batch;
+  if (B < 1 || B > XB_MAX_BATCH) return fail(XB_ERR_INVALID, "batch must be 1..8");
+  int dev = 0;
+  XB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kStaticMaxDevices) return fail(XB_ERR_UNSUPPORTED, "device ordinal too large");
+  StaticDevice sd;
+  {
+    // One-time set-up per device, with that device current: look up the device address of the
+    // static array (host code may not use the symbol's host-side name as a device address).
+    std::lock_guard<std::mutex> lock(mu);
+    StaticDevice &d = devices[dev];
+    if (!d.ready) {
+      void *ptr = nullptr;
+      XB_CUDA(cudaGetSymbolAddress(&ptr, g_static_scratch));
+      int sms = 0;
+      XB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+      d.base = static_cast<unsigned char *>(ptr);
+      d.num_sms = sms;
+      d.ready = true;
+    }
+    sd = d;
+  }
+  const size_t ws_bytes = ws_layout(g, B, sd.num_sms).total;
+  const size_t ws_room = kStaticScratchBytes - kStaticWsOffset;
+  if (ws_bytes > ws_room)
+    return fail(XB_ERR_INVALID,
+                "xb_decode_step_static: this model and batch need " + std::to_string(ws_bytes) +
+                    " bytes of scratch, more than the " + std::to_string(ws_room) +
+                    " bytes of the static array (use xb_decode_step with a workspace)");
+  if ((size_t)(g.rotary_dim / 2) * sizeof(float) > kStaticRopeBytes)
+    return fail(XB_ERR_INVALID, "rotary_dim too large for the static RoPE table");
+  cudaStream_t st = (cudaStream_t)stream;
+  unsigned char *table = sd.base;
+  unsigned char *rope = sd.base + kStaticTableBytes;
+  unsigned char *ws = sd.base + kStaticWsOffset;
+  // Same weight-pointer rules as xb_model_create: present, and 16-byte aligned where the kernel
+  // streams them with bulk copies.
+  if (!weights->embed || !weights->final_norm || !weights->lm_head || ((uintptr_t)weights->lm_head & 15))
+    return fail(XB_ERR_INVALID, "embed, final_norm and a 16-byte aligned lm_head are required");
+  for (int l = 0; l < g.num_layers; ++l) {
+    const XbLayerWeights &w = weights->layers[l];
+    const bool delta = g.layer_kind[l] == XB_LAYER_DELTANET;
+    const void *need[] = {w.input_norm, w.post_norm, w.gate, w.up, w.down,
+                          delta ? w.in_qkv : w.q_proj, delta ? w.in_z : w.k_proj,
+                          delta ? w.in_b : w.v_proj, delta ? w.out_proj : w.o_proj,
+                          delta ? w.in_a : w.q_norm, delta ? w.conv_w : w.k_norm,
+                          delta ? w.a_log : w.input_norm, delta ? w.dt_bias : w.input_norm,
+                          delta ? w.gnorm : w.input_norm};
+    for (int i = 0; i < 14; ++i) {
+      if (!need[i]) return fail(XB_ERR_INVALID, "missing weight pointer in layer " + std::to_string(l));
+      if (i < 10 && ((uintptr_t)need[i] & 15))
+        return fail(XB_ERR_INVALID, "projection weights must be 16-byte aligned");
+    }
+  }
+  // Stage the weight table and RoPE frequencies into the static array (stream-ordered copies
+  // from host memory; no allocation). Every call rewrites them.
+  float inv[kStaticRopeBytes / sizeof(float)];
+  if (g.rope_inv_freq) memcpy(inv, g.rope_inv_freq, sizeof(float) * (g.rotary_dim / 2));
+  else xb_rope_inv_freq(g.rope_theta, g.rotary_dim, inv);
+  XB_CUDA(cudaMemcpyAsync(table, weights->layers, sizeof(XbLayerWeights) * g.num_layers,
+                          cudaMemcpyHostToDevice, st));
+  XB_CUDA(cudaMemcpyAsync(rope, inv, sizeof(float) * (g.rotary_dim / 2), cudaMemcpyHostToDevice, st));
+  // The array keeps the previous call's contents; the barrier / error / completion words must
+  // start at zero, so clear them before every launch.
+  XB_CUDA(cudaMemsetAsync(ws, 0, CTL_WORDS * 4, st));
+  XbModel m;
+  m.g = g;
+  m.w = *weights;
+  m.d_layers = reinterpret_cast<XbLayerWeights *>(table);
+  m.d_inv_freq = reinterpret_cast<float *>(rope);
+  m.device = dev;
+  m.num_sms = sd.num_sms;
+  // Same validation and launch as xb_decode_step; the model is a host-stack view (the weight
+  // pointers of `weights` must also satisfy xb_model_create's alignment rules).
+  rc = xb_decode_step(&m, args, ws, ws_room, stream);
+  if (rc) return rc;
+  if (device_error) {
+    unsigned err = 0;
+    XB_CUDA(cudaStreamSynchronize(st));
+    XB_CUDA(cudaMemcpy(&err, ws + CTL_ERR * 4, 4, cudaMemcpyDeviceToHost));
+    *device_error = (int32_t)err;
+    if (err) return fail(XB_ERR_DEVICE, "device-side error code " + std::to_string(err));
+  }
+  return XB_OK;
+}
