@@ -155,9 +155,9 @@ int xb_rope_inv_freq(float theta, int32_t rotary_dim, float *out);
 
 /* Stage trace for performance work (the reference has no in-process tracer; it profiles with
  * external tools). While a device buffer is set, every xb_decode_step launch writes, per CTA,
- * (2 * 512 + 4) u64 words: %globaltimer at each stage's barrier arrival and release, the
- * kernel end time, the consumers' total ring-slot wait, the stage count and the producer's
- * busy time. Pass NULL to switch tracing off. The buffer must hold 1024 CTAs' worth. */
+ * (3 * 512 + 8) u64 words: %globaltimer at each stage's barrier arrival, release and end of
+ * prologue, then the kernel end time, the consumers' total ring-slot wait, the stage count, the
+ * producer's busy time, its total wait for free slots and the number of tiles it issued. Pass NULL to switch tracing off. The buffer must hold 1024 CTAs' worth. */
 int xb_debug_trace(void *device_buffer, size_t bytes);
 
 const char *xb_last_error(void);

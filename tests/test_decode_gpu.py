@@ -56,15 +56,22 @@ class LazyWeights(dict):
         return self[key] if key in self.sd else default
 
 
-def check_logits(got, want, where):
+# Full-width shallow configs (hidden 1024/2560, 3 DeltaNet + 1 attention layer) already sit at
+# a measured noise floor: the oracle against itself with fp64 instead of fp32 GEMV sums differs
+# by up to 0.048 max-abs and cosine 0.99991. Bound: twice that, absolute.
+FULLW_MAX_ABS = 0.1
+FULLW_COS = 0.9998
+
+
+def check_logits(got, want, where, ulps=1, cos_min=LOGIT_COS, max_abs=LOGIT_MAX_ABS):
     """North-star bar per element: |got - want| <= 2e-2, widened by one bf16 ulp of the
     reference value (2^-7 |want|) because bf16 logits above 2.56 have an ulp larger than 2e-2;
     plus cosine >= 0.9999 over the row."""
     got, want = got.float().cpu(), want.float().cpu()
-    excess = ((got - want).abs() - (LOGIT_MAX_ABS + want.abs() * 2.0 ** -7)).max().item()
+    excess = ((got - want).abs() - (max_abs + ulps * want.abs() * 2.0 ** -7)).max().item()
     err = (got - want).abs().max().item()
     cos = O.cosine(got, want)
-    assert excess <= 0 and cos >= LOGIT_COS, f"{where}: max abs {err}, cosine {cos}"
+    assert excess <= 0 and cos >= cos_min, f"{where}: max abs {err}, cosine {cos}"
 
 
 def run_schedule_gpu(eng, g, schedule, device, rows_alloc=8):
@@ -150,7 +157,8 @@ def test_full_width_matches_oracle(name, cuda_device):
     got, toks, state, _ = run_schedule_gpu(eng, g, sched, cuda_device)
     want, ostate = run_schedule_oracle(g, W, sched, 64)
     for s in range(len(sched)):
-        check_logits(got[s, 0], want[s, 0], f"{name} step {s}")
+        check_logits(got[s, 0], want[s, 0], f"{name} step {s}", cos_min=FULLW_COS,
+                     max_abs=FULLW_MAX_ABS)
         assert int(toks[s, 0]) == int(torch.argmax(got[s, 0].float()))
     for i, (a, b) in enumerate(zip(state, ostate)):
         n = len(sched)

@@ -25,7 +25,7 @@ EXPORTED = (
     "xb_abi_version", "xb_decode_step_static", "xb_debug_trace",
 )
 TRACE_STAGES = 512
-TRACE_STRIDE = 2 * TRACE_STAGES + 4
+TRACE_STRIDE = 3 * TRACE_STAGES + 8
 TRACE_BYTES = TRACE_STRIDE * 8 * 1024
 STATIC_SCRATCH_BYTES = 4 << 20
 

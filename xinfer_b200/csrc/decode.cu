@@ -38,13 +38,16 @@ constexpr int kCT = kWarps * 32;          // consumer threads
 constexpr int kThreads = kCT + 32;        // + producer warp
 constexpr int kSlot = 32768;              // ring slot bytes
 constexpr int kMaxSlots = 8;
-constexpr int kHdrBytes = 256;
+constexpr int kHdrBytes = 512;
 constexpr int kRedFloats = 1024;
-constexpr int kUOffset = kHdrBytes + kRedFloats * 4;  // 4352, 128-aligned
+constexpr int kUOffset = kHdrBytes + kRedFloats * 4;  // 4608, 128-aligned
 constexpr int kSmemLimit = 232448;                     // 227 KB opt-in per CTA
+// layout of the per-CTA float scratch `red` during GEMV stages
+constexpr int RED_RESID = 64;   // [NB][rows of this CTA] residual rows (<= 256)
+constexpr int RED_PART = 512;   // [2][kWarps][2][NB][2] split-K partials
 
 // control words in the workspace (each on its own 128-byte line)
-enum { CTL_COUNT = 0, CTL_GEN = 32, CTL_ERR = 64, CTL_DONE = 96, CTL_WORDS = 128 };
+enum { CTL_ERR = 64, CTL_DONE = 96, CTL_BAR = 128, CTL_WORDS = 128 + 8 * 32 };
 // device error codes
 enum { DERR_BARRIER = 1, DERR_RING_FULL = 2, DERR_RING_EMPTY = 3, DERR_TOKEN = 4, DERR_DRAIN = 5 };
 
@@ -76,7 +79,7 @@ struct StepParams {
   unsigned long long *trace;
 };
 constexpr int kTraceStages = 512;
-constexpr int kTraceStride = 2 * kTraceStages + 4;  // u64 words per CTA
+constexpr int kTraceStride = 3 * kTraceStages + 8;  // u64 words per CTA
 
 struct SmemHdr {
   uint64_t full[kMaxSlots];
@@ -181,6 +184,7 @@ struct Producer {
   unsigned phase = 0;
   int issued = 0;
   bool stop = false;
+  unsigned long long empty_wait = 0;  // ns waiting for free slots (trace)
 
   __device__ Producer(const StepParams &p_, SmemHdr *h, char *r) : p(p_), hdr(h), ring(r) {
     policy = policy_evict_first();
@@ -191,6 +195,11 @@ struct Producer {
     // (the second condition only matters after an abort, when consumers release unread slots).
     uint64_t t0 = 0;
     unsigned spins = 0;
+    const uint64_t tw = p.trace ? globaltimer() : 0;
+    struct Acc {
+      const StepParams &p; unsigned long long &acc; uint64_t tw;
+      __device__ ~Acc() { if (p.trace) acc += globaltimer() - tw; }
+    } acc_guard{p, empty_wait, tw};
     while (!mbar_try_wait(&hdr->empty[slot], phase ^ 1u) ||
            (issued >= p.nslots && !mbar_try_wait(&hdr->full[slot], phase ^ 1u))) {
       if ((++spins & 63u) == 0) {
@@ -258,6 +267,7 @@ template <int NB> struct Consumer {
   bool first = true;      // first stage of the step needs no barrier
   bool h_ready = false;   // residual stream in p.h (false: still the embedding rows)
   int sidx = 0;           // stage counter (trace)
+  int nbar = 0;           // grid barriers passed in this launch
   unsigned long long full_wait = 0;  // ns spent waiting for ring slots (trace, tid 0)
   // running argmax for the lm_head stage (lane b keeps batch row b)
   float am_v = -INFINITY;
@@ -282,32 +292,40 @@ template <int NB> struct Consumer {
     *reinterpret_cast<volatile int *>(&hdr->abort) = 1;
   }
 
+  // Grid barrier: one release-reduction per CTA onto one of eight counters (spreading the
+  // atomic traffic over eight L2 lines), then lanes 0-7 of warp 0 poll the eight counters with
+  // acquire loads until their sum reaches (barriers so far) x (CTAs). The counters are monotonic
+  // within a launch and reset by the last CTA to finish the step.
   __device__ void grid_sync() {
     csync();
-    if (tid == 0 && !aborted()) {
+    ++nbar;
+    if (warp == 0 && !aborted()) {
       unsigned *ctrl = p.ctrl;
-      const unsigned gen = ld_acquire(ctrl + CTL_GEN);
-      __threadfence();
-      const unsigned prev = atomicAdd(ctrl + CTL_COUNT, 1u);
-      if (prev == (unsigned)p.ncta - 1u) {
-        atomicExch(ctrl + CTL_COUNT, 0u);
-        __threadfence();
-        st_release(ctrl + CTL_GEN, gen + 1u);
-      } else {
-        uint64_t t0 = globaltimer();
-        unsigned spins = 0;
-        while (ld_acquire(ctrl + CTL_GEN) == gen) {
-          if ((++spins & 255u) == 0) {
-            if (ld_volatile(ctrl + CTL_ERR)) break;
-            if (globaltimer() - t0 > kWaitLimitNs) {
+      if (lane == 0) red_release_add(ctrl + CTL_BAR + (blockIdx.x & 7) * 32, 1u);
+      const unsigned target = (unsigned)nbar * (unsigned)p.ncta;
+      const uint64_t t0 = globaltimer();
+      unsigned spins = 0;
+      for (;;) {
+        unsigned v = lane < 8 ? ld_acquire(ctrl + CTL_BAR + lane * 32) : 0u;
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        if (__shfl_sync(0xffffffffu, v, 0) >= target) break;
+        if ((++spins & 127u) == 0) {
+          int stop = 0;
+          if (lane == 0) {
+            if (ld_volatile(ctrl + CTL_ERR)) stop = 1;
+            else if (globaltimer() - t0 > kWaitLimitNs) {
               atomicCAS(ctrl + CTL_ERR, 0u, (unsigned)DERR_BARRIER);
-              break;
+              stop = 1;
             }
+          }
+          if (__shfl_sync(0xffffffffu, stop, 0)) {
+            if (lane == 0) *reinterpret_cast<volatile int *>(&hdr->abort) = 1;
+            break;
           }
         }
       }
-      __threadfence();
-      if (ld_volatile(ctrl + CTL_ERR)) *reinterpret_cast<volatile int *>(&hdr->abort) = 1;
     }
     csync();
   }
@@ -315,18 +333,24 @@ template <int NB> struct Consumer {
   __device__ void stage_begin() {
     unsigned long long *tr = p.trace ? p.trace + (size_t)blockIdx.x * kTraceStride : nullptr;
     const int si = sidx < kTraceStages ? sidx : kTraceStages - 1;
-    if (tr && tid == 0) tr[2 * si] = globaltimer();
+    if (tr && tid == 0) tr[3 * si] = globaltimer();
     if (first) first = false;
     else grid_sync();
-    if (tr && tid == 0) tr[2 * si + 1] = globaltimer();
+    if (tr && tid == 0) tr[3 * si + 1] = tr[3 * si + 2] = globaltimer();
     ++sidx;
+  }
+  __device__ void trace_mark() {  // end of a GEMV stage's prologue
+    if (p.trace && tid == 0) {
+      const int si = (sidx - 1) < kTraceStages ? sidx - 1 : kTraceStages - 1;
+      p.trace[(size_t)blockIdx.x * kTraceStride + 3 * si + 2] = globaltimer();
+    }
   }
   __device__ void trace_end() {
     if (p.trace && tid == 0) {
       unsigned long long *tr = p.trace + (size_t)blockIdx.x * kTraceStride;
-      tr[2 * kTraceStages] = globaltimer();
-      tr[2 * kTraceStages + 1] = full_wait;
-      tr[2 * kTraceStages + 2] = (unsigned long long)sidx;
+      tr[3 * kTraceStages] = globaltimer();
+      tr[3 * kTraceStages + 1] = full_wait;
+      tr[3 * kTraceStages + 2] = (unsigned long long)sidx;
     }
   }
 
@@ -334,12 +358,7 @@ template <int NB> struct Consumer {
     if (aborted()) return nullptr;
     uint64_t t0 = 0;
     unsigned spins = 0;
-    if (p.trace && tid == 0 && !mbar_try_wait(&hdr->full[slot], phase)) {
-      const uint64_t a = globaltimer();
-      while (!mbar_try_wait(&hdr->full[slot], phase) && globaltimer() - a < kWaitLimitNs) {
-      }
-      full_wait += globaltimer() - a;
-    }
+    const uint64_t tw = (p.trace && tid == 0) ? globaltimer() : 0;
     while (!mbar_try_wait(&hdr->full[slot], phase)) {
       if ((++spins & 63u) == 0) {
         if (aborted()) return nullptr;
@@ -355,6 +374,7 @@ template <int NB> struct Consumer {
         }
       }
     }
+    if (p.trace && tid == 0) full_wait += globaltimer() - tw;
     return ring + (size_t)slot * kSlot;
   }
   __device__ void release() {
@@ -363,27 +383,56 @@ template <int NB> struct Consumer {
     if (++slot == p.nslots) { slot = 0; phase ^= 1u; }
   }
 
-  // Residual-stream row b, element e (embedding row before the first residual update).
+  // 16 bytes (8 bf16) of residual-stream row b at element e (embedding row before the first
+  // residual update, which is read-only; afterwards the stream written by other CTAs).
+  __device__ __forceinline__ uint4 hchunk(int b, int e) const {
+    if (!h_ready) return ldnc_u4(p.embed + (size_t)token_id(p, b) * p.H + e);
+    return ldcg_u4(p.h + (size_t)b * p.H + e);
+  }
   __device__ __forceinline__ float hval(int b, int e) const {
-    if (!h_ready) {
-      const long long id = token_id(p, b);
-      return bf(p.embed[(size_t)id * p.H + e]);
-    }
+    if (!h_ready) return bf(p.embed[(size_t)token_id(p, b) * p.H + e]);
     return bf(ldcg_bf(p.h + (size_t)b * p.H + e));
+  }
+
+  // Residual rows [lo, hi) of this CTA, read before the tile loop (RESID epilogues).
+  __device__ __forceinline__ float resid_load(int lo, int hi) const {
+    const int n = hi - lo;
+    const int b = tid / max(n, 1), r = tid - b * max(n, 1);
+    return (n > 0 && b < NB && b < p.B) ? hval(b, lo + r) : 0.f;
+  }
+  __device__ __forceinline__ void resid_store(float v, int lo, int hi) {
+    const int n = hi - lo;
+    if (n > 0 && tid < NB * n) red[RED_RESID + tid] = v;
   }
 
   // RMSNorm of the residual stream into the activation buffer (bf16 [NB][H]).
   //  Qwen3   : w * bf16(x * rsqrt(mean(x^2) + eps))        (HF Qwen3RMSNorm)
   //  Qwen3.5 : bf16(x * rsqrt(mean(x^2) + eps) * (1 + w))   (HF Qwen3_5RMSNorm)
+  // All loads are issued before any use: one round trip to L2 per stage.
   __device__ void norm_prologue(const bf16 *w) {
-    bf16 *act = reinterpret_cast<bf16 *>(U);
-    const int H = p.H;
+    uint4 *act = reinterpret_cast<uint4 *>(U);
+    const int H = p.H, nc = H / 8;
+    constexpr int MAXC = 2;  // H <= 2 * 256 * 8
+    uint4 xv[NB][MAXC], wv[MAXC];
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = tid + i * kCT;
+      wv[i] = c < nc ? ldnc_u4(w + c * 8) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int b = 0; b < NB; ++b)
+        xv[b][i] = (c < nc && b < p.B) ? hchunk(b, c * 8) : make_uint4(0, 0, 0, 0);
+    }
     float ss[NB];
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
       ss[b] = 0.f;
-      if (b < p.B)
-        for (int e = tid; e < H; e += kCT) { const float x = hval(b, e); ss[b] = fmaf(x, x, ss[b]); }
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        float x[8];
+        unpack8(xv[b][i], x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss[b] = fmaf(x[e], x[e], ss[b]);
+      }
       ss[b] = warp_sum(ss[b]);
     }
     if (lane == 0)
@@ -393,69 +442,92 @@ template <int NB> struct Consumer {
     const bool q35 = p.family == XB_FAMILY_QWEN35;
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
-      if (b < p.B) {
-        float tot = 0.f;
-        for (int i = 0; i < kWarps; ++i) tot += red[i * NB + b];
-        const float r = rsqrtf(tot / (float)H + p.eps);
-        for (int e = tid; e < H; e += kCT) {
-          const float x = hval(b, e), wv = bf(w[e]);
-          const float y = q35 ? rbf(x * r * (1.f + wv)) : rbf(wv * rbf(x * r));
-          act[b * H + e] = tobf(y);
-        }
-      } else {
-        for (int e = tid; e < H; e += kCT) act[b * H + e] = tobf(0.f);
+      float tot = 0.f;
+#pragma unroll
+      for (int i = 0; i < kWarps; ++i) tot += red[i * NB + b];
+      const float r = rsqrtf(tot / (float)H + p.eps);
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = tid + i * kCT;
+        if (c >= nc) continue;
+        float x[8], wf[8], y[8];
+        unpack8(xv[b][i], x);
+        unpack8(wv[i], wf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          y[e] = (b < p.B) ? (q35 ? x[e] * r * (1.f + wf[e]) : wf[e] * rbf(x[e] * r)) : 0.f;
+        act[b * nc + c] = make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]),
+                                     pack2(y[6], y[7]));
       }
     }
-    csync();
   }
 
   // Copy a bf16 scratch vector [B][K] (stride ld) produced this launch into the activations.
   __device__ void copy_prologue(const bf16 *src, int K, int ld) {
-    bf16 *act = reinterpret_cast<bf16 *>(U);
-    const int n8 = K / 8;
+    uint4 *act = reinterpret_cast<uint4 *>(U);
+    const int nc = K / 8;
+    constexpr int MAXC = 5;  // K <= 5 * 256 * 8
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
-      uint4 *dst = reinterpret_cast<uint4 *>(act + b * K);
-      for (int j = tid; j < n8; j += kCT)
-        dst[j] = (b < p.B) ? ldcg_u4(src + (size_t)b * ld + j * 8) : make_uint4(0, 0, 0, 0);
+      uint4 v[MAXC];
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = tid + i * kCT;
+        v[i] = (c < nc && b < p.B) ? ldcg_u4(src + (size_t)b * ld + c * 8) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = tid + i * kCT;
+        if (c < nc) act[b * nc + c] = v[i];
+      }
     }
-    csync();
   }
 
   // Gated RMSNorm of the DeltaNet core output (HF Qwen3_5RMSNormGated, as called in
   // compiler/qwen35/adapters/delta.py:46-47): y = bf16( bf16(w * bf16(x * r)) * silu(z) ).
+  // Each thread derives its head's 1/rms from the eight per-tile partial sums itself.
   __device__ void gated_norm_prologue(const bf16 *w) {
-    bf16 *act = reinterpret_cast<bf16 *>(U);
-    const int K = p.HV * p.DK, DK = p.DK;
+    uint4 *act = reinterpret_cast<uint4 *>(U);
+    const int K = p.HV * p.DK, nc = K / 8, DK = p.DK;
     const int zoff = 2 * p.HK * p.DK + p.HV * p.DK;
-    float *rs = red;  // [NB][HV] inverse rms
-    for (int i = tid; i < NB * p.HV; i += kCT) {
-      const int b = i / p.HV, h = i % p.HV;
-      float r = 0.f;
-      if (b < p.B) {
-        float tot = 0.f;
-        for (int t = 0; t < 8; ++t) tot += ldcg_f(p.ssq + ((size_t)b * p.HV + h) * 8 + t);
-        r = rsqrtf(tot / (float)DK + p.eps);
-      }
-      rs[i] = r;
-    }
-    csync();
+    constexpr int MAXC = 2;  // K <= 4096
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
-      for (int e = tid; e < K; e += kCT) {
-        float y = 0.f;
-        if (b < p.B) {
-          const float x = bf(ldcg_bf(p.core + (size_t)b * K + e));
-          const float r = rs[b * p.HV + e / DK];
-          const float n = rbf(bf(w[e % DK]) * rbf(x * r));
-          const float z = bf(ldcg_bf(p.proj + (size_t)b * p.pstride + zoff + e));
-          const float s = z / (1.f + expf(-z));
-          y = rbf(n * s);
+      uint4 xv[MAXC], zv[MAXC], wv[MAXC];
+      float part[MAXC][8];
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = tid + i * kCT;
+        const bool ok = c < nc && b < p.B;
+        xv[i] = ok ? ldcg_u4(p.core + (size_t)b * K + c * 8) : make_uint4(0, 0, 0, 0);
+        zv[i] = ok ? ldcg_u4(p.proj + (size_t)b * p.pstride + zoff + c * 8) : make_uint4(0, 0, 0, 0);
+        wv[i] = c < nc ? ldnc_u4(w + (c * 8) % DK) : make_uint4(0, 0, 0, 0);
+        const int h = (c * 8) / DK;
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+          part[i][t] = ok ? ldcg_f(p.ssq + ((size_t)b * p.HV + h) * 8 + t) : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = tid + i * kCT;
+        if (c >= nc) continue;
+        float tot = 0.f;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) tot += part[i][t];
+        const float r = rsqrtf(tot / (float)DK + p.eps);
+        float x[8], z[8], wf[8], y[8];
+        unpack8(xv[i], x);
+        unpack8(zv[i], z);
+        unpack8(wv[i], wf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float n = rbf(wf[e] * rbf(x[e] * r));
+          y[e] = (b < p.B) ? n * (z[e] / (1.f + expf(-z[e]))) : 0.f;
         }
-        act[b * K + e] = tobf(y);
+        act[b * nc + c] = make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]),
+                                     pack2(y[6], y[7]));
       }
     }
-    csync();
   }
 
   // Next conv window per channel: [conv[1], conv[2], conv[3], x] for active rows, unchanged for
@@ -481,64 +553,133 @@ template <int NB> struct Consumer {
   }
 
   // ---- GEMV tile loop ----------------------------------------------------------------------
+  // A warp handles a pair of rows of the tile (two independent FMA chains; gate/up tiles carry
+  // four), over all of K or, when the tile has fewer than 16 rows, over 1/S of K with the S
+  // partial sums combined through shared memory. Lanes 0..NB-1 run the epilogue of the first
+  // row for batch rows 0..NB-1, lanes 16..16+NB-1 that of the second row.
   __device__ void gemv(int l, int stage) {
     stage_begin();
     const Gemv g = make_gemv(p, l, stage);
     const XbLayerWeights *w = (stage == ST_LMHEAD) ? nullptr : &p.layers[l];
+    int lo, hi;
+    cta_range(g.N, blockIdx.x, p.ncta, lo, hi);
     int epi = EPI_STORE;
     switch (stage) {
     case ST_IN_DELTA:
-    case ST_QKV: norm_prologue((const bf16 *)w->input_norm); epi = EPI_STORE; break;
-    case ST_OUT_DELTA:
+    case ST_QKV: norm_prologue((const bf16 *)w->input_norm); break;
+    case ST_OUT_DELTA: {
+      const float rv = resid_load(lo, hi);
       conv_state_update(l);
       gated_norm_prologue((const bf16 *)w->gnorm);
+      resid_store(rv, lo, hi);
       epi = EPI_RESID;
       break;
-    case ST_O: copy_prologue(p.att_out, g.K, p.HQ * p.D); epi = EPI_RESID; break;
+    }
+    case ST_O: {
+      const float rv = resid_load(lo, hi);
+      copy_prologue(p.att_out, g.K, p.HQ * p.D);
+      resid_store(rv, lo, hi);
+      epi = EPI_RESID;
+      break;
+    }
     case ST_GATEUP: norm_prologue((const bf16 *)w->post_norm); epi = EPI_GATEUP; break;
-    case ST_DOWN: copy_prologue(p.act, g.K, p.I); epi = EPI_RESID; break;
+    case ST_DOWN: {
+      const float rv = resid_load(lo, hi);
+      copy_prologue(p.act, g.K, p.I);
+      resid_store(rv, lo, hi);
+      epi = EPI_RESID;
+      break;
+    }
     case ST_LMHEAD: norm_prologue(p.final_norm); epi = EPI_LOGITS; break;
     }
+    csync();
+    trace_mark();
     const bf16 *act = reinterpret_cast<const bf16 *>(U);
-    int lo, hi;
-    cta_range(g.N, blockIdx.x, p.ncta, lo, hi);
     const int R = tile_rows(g);
     const int K = g.K, n8 = K / 8;
-    for (int r0 = lo; r0 < hi; r0 += R) {
+    const size_t rowb = (size_t)K * 2;
+    const int bsel = lane & 15;
+    const bool second = lane >= 16;
+    int parity = 0;
+    for (int r0 = lo; r0 < hi; r0 += R, parity ^= 1) {
       const int n = min(R, hi - r0);
+      const int pairs = (n + 1) >> 1;
+      int S = 1;
+      while (S < kWarps && pairs * S * 2 <= kWarps) S <<= 1;
       const char *slotp = wait_full();
-      for (int i = warp; slotp && i < n; i += kWarps) {
-        float acc[NB], acc2[NB];
+      const int seg = warp % S;
+      // S > 1 only when all pairs fit in one pass (pairs * S <= kWarps)
+      for (int pbase = 0; pbase < pairs; pbase += kWarps / S) {
+        const int pair = pbase + warp / S;
+        const bool active = slotp != nullptr && pair < pairs;
+        float a0[NB], a1[NB], c0[NB], c1[NB];
 #pragma unroll
-        for (int b = 0; b < NB; ++b) { acc[b] = 0.f; acc2[b] = 0.f; }
-        const uint4 *w4 = reinterpret_cast<const uint4 *>(slotp + (size_t)i * K * 2);
-        const uint4 *u4 = reinterpret_cast<const uint4 *>(slotp + (size_t)(n + i) * K * 2);
-        for (int j = lane; j < n8; j += 32) {
-          float wf[8], uf[8];
-          unpack8(w4[j], wf);
-          if (g.paired) unpack8(u4[j], uf);
+        for (int b = 0; b < NB; ++b) { a0[b] = a1[b] = c0[b] = c1[b] = 0.f; }
+        if (active) {
+          const int rA = 2 * pair, rB = min(rA + 1, n - 1);
+          const uint4 *wA = reinterpret_cast<const uint4 *>(slotp + rA * rowb);
+          const uint4 *wB = reinterpret_cast<const uint4 *>(slotp + rB * rowb);
+          const uint4 *uA = reinterpret_cast<const uint4 *>(slotp + (n + rA) * rowb);
+          const uint4 *uB = reinterpret_cast<const uint4 *>(slotp + (n + rB) * rowb);
+          const int cb = (n8 * seg) / S, ce = (n8 * (seg + 1)) / S;
+          const uint4 *act4 = reinterpret_cast<const uint4 *>(act);
+          if (g.paired) {
+#pragma unroll 2
+            for (int j = cb + lane; j < ce; j += 32) {
+              const uint4 wa = wA[j], wb = wB[j], ua = uA[j], ub = uB[j];
+#pragma unroll
+              for (int b = 0; b < NB; ++b) {
+                const uint4 x = act4[b * n8 + j];
+                a0[b] = dot8_bf16(wa, x, a0[b]);
+                c0[b] = dot8_bf16(wb, x, c0[b]);
+                a1[b] = dot8_bf16(ua, x, a1[b]);
+                c1[b] = dot8_bf16(ub, x, c1[b]);
+              }
+            }
+          } else {
+#pragma unroll 4
+            for (int j = cb + lane; j < ce; j += 32) {
+              const uint4 wa = wA[j], wb = wB[j];
+#pragma unroll
+              for (int b = 0; b < NB; ++b) {
+                const uint4 x = act4[b * n8 + j];
+                a0[b] = dot8_bf16(wa, x, a0[b]);
+                c0[b] = dot8_bf16(wb, x, c0[b]);
+              }
+            }
+          }
 #pragma unroll
           for (int b = 0; b < NB; ++b) {
-            float xf[8];
-            unpack8(reinterpret_cast<const uint4 *>(act + b * K)[j], xf);
+            a0[b] = warp_sum(a0[b]);
+            c0[b] = warp_sum(c0[b]);
+            if (g.paired) { a1[b] = warp_sum(a1[b]); c1[b] = warp_sum(c1[b]); }
+          }
+        }
+        float v = 0.f, v2 = 0.f;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc[b] = fmaf(wf[e], xf[e], acc[b]);
-            if (g.paired) {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) acc2[b] = fmaf(uf[e], xf[e], acc2[b]);
+        for (int b = 0; b < NB; ++b)
+          if (bsel == b) { v = second ? c0[b] : a0[b]; v2 = second ? c1[b] : a1[b]; }
+        if (S > 1) {
+          float *part = red + RED_PART + parity * 256;  // [warp][2 rows][NB][2]
+          if (active && bsel < NB) {
+            float *q = part + ((warp * 2 + (second ? 1 : 0)) * NB + bsel) * 2;
+            q[0] = v;
+            q[1] = v2;
+          }
+          csync();
+          if (active && seg == 0 && bsel < NB) {
+            v = v2 = 0.f;
+            for (int sgi = 0; sgi < S; ++sgi) {
+              const float *q = part + (((pair * S + sgi) * 2 + (second ? 1 : 0)) * NB + bsel) * 2;
+              v += q[0];
+              v2 += q[1];
             }
           }
         }
-#pragma unroll
-        for (int b = 0; b < NB; ++b) {
-          acc[b] = warp_sum(acc[b]);
-          if (g.paired) acc2[b] = warp_sum(acc2[b]);
+        if (active && seg == 0 && bsel < NB && bsel < p.B) {
+          const int row = 2 * pair + (second ? 1 : 0);
+          if (row < n) epilogue(epi, bsel, r0 + row, v, v2, lo, hi - lo);
         }
-        float v = acc[0], v2 = acc2[0];
-#pragma unroll
-        for (int b = 1; b < NB; ++b)
-          if (lane == b) { v = acc[b]; v2 = acc2[b]; }
-        if (lane < NB && lane < p.B) epilogue(epi, lane, r0 + i, v, v2);
       }
       release();
     }
@@ -546,13 +687,14 @@ template <int NB> struct Consumer {
     if (epi == EPI_LOGITS) argmax_finish();
   }
 
-  __device__ __forceinline__ void epilogue(int epi, int b, int row, float v, float v2) {
+  __device__ __forceinline__ void epilogue(int epi, int b, int row, float v, float v2, int lo,
+                                           int nres) {
     switch (epi) {
     case EPI_STORE:
       p.proj[(size_t)b * p.pstride + row] = tobf(v);
       break;
     case EPI_RESID: {
-      const float hv = hval(b, row);
+      const float hv = red[RED_RESID + b * nres + (row - lo)];
       p.h[(size_t)b * p.H + row] = tobf(hv + rbf(v));
       break;
     }
@@ -571,19 +713,25 @@ template <int NB> struct Consumer {
     }
   }
 
-  // Per-CTA argmax -> workspace; the last CTA to finish reduces all CTAs (ordered by rows).
+  // Per-CTA argmax -> workspace; the last CTA to finish reduces all CTAs, writes the tokens and
+  // resets the barrier counters and its own ticket for the next launch.
   __device__ void argmax_finish() {
-    float *sv = red;                       // [kWarps][NB]
-    int *si = reinterpret_cast<int *>(red + kWarps * NB);
-    if (lane < NB) { sv[warp * NB + lane] = am_v; si[warp * NB + lane] = am_i; }
+    float *sv = red;                                  // [kWarps][2][NB]
+    int *si = reinterpret_cast<int *>(red + 2 * kWarps * NB);
+    const int bsel = lane & 15;
+    if (bsel < NB) {
+      const int k = (warp * 2 + (second_half() ? 1 : 0)) * NB + bsel;
+      sv[k] = am_v;
+      si[k] = am_i;
+    }
     csync();
     if (tid < NB && tid < p.B) {
-      float bv = sv[tid];
-      int bi = si[tid];
-      for (int i = 1; i < kWarps; ++i)
-        if (argmax_better(sv[i * NB + tid], si[i * NB + tid], bv, bi)) {
-          bv = sv[i * NB + tid];
-          bi = si[i * NB + tid];
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int k = 0; k < 2 * kWarps; ++k)
+        if (argmax_better(sv[k * NB + tid], si[k * NB + tid], bv, bi)) {
+          bv = sv[k * NB + tid];
+          bi = si[k * NB + tid];
         }
       p.am_v[blockIdx.x * XB_MAX_BATCH + tid] = bv;
       p.am_i[blockIdx.x * XB_MAX_BATCH + tid] = bi;
@@ -607,12 +755,16 @@ template <int NB> struct Consumer {
         }
         p.tokens[tid] = bi;
       }
+      // every CTA has passed its last grid barrier before taking a ticket
+      if (tid < 8) p.ctrl[CTL_BAR + tid * 32] = 0u;
       if (tid == 0) atomicExch(p.ctrl + CTL_DONE, 0u);
     }
   }
+  __device__ __forceinline__ bool second_half() const { return lane >= 16; }
 
   // ---- Gated DeltaNet recurrent step (compiler/qwen35/kernels/recurrent.py:20-124) ---------
-  // Work item = (row b, value head h, 16-column tile t of the 128x128 state).
+  // Work item = (row b, value head h, 16-column tile t of the 128x128 state). Every global load
+  // of an item (state slice, conv windows and taps, projections, gate scalars) is issued up front.
   __device__ void delta(int l) {
     stage_begin();
     const XbLayerWeights &w = p.layers[l];
@@ -622,95 +774,107 @@ template <int NB> struct Consumer {
     const int tiles = DK / 16;
     const int items = p.B * HV * tiles;
     const bf16 *cw = (const bf16 *)w.conv_w;
-    float *qk = red;              // [2*DK]  (q | k)
-    float *vv = red + 2 * DK;     // [16]
-    float *part = red + 2 * DK + 16;   // [kWarps][16]
-    float *misc = red + 2 * DK + 16 + kWarps * 16;  // [8]
+    float *qk = red;               // [2*DK]  (q | k)
+    float *vv = red + 256;         // [16]
+    float *pn = red + 272;         // [kWarps] norm partials
+    float *gt = red + 280;         // beta, decay
+    float *pp = red + 288;         // [kWarps][16] prediction partials
+    float *po = red + 416;         // [kWarps][16] output partials
     const bf16 *conv_in_all = (const bf16 *)p.sa[l];
     const float *rec_in_all = (const float *)p.sb[l];
     float *rec_out_all = (float *)p.sd[l];
+    const int c = lane & 15;
+    const int rbase = warp * 16 + (lane >> 4) * 8;
     for (int item = blockIdx.x; item < items; item += p.ncta) {
       const int b = item / (HV * tiles);
       const int h = (item / tiles) % HV;
       const int t = item % tiles;
       const int kh = h / group;
-      const bf16 *cin = conv_in_all + (size_t)b * CH * CW;
       const float *S_in = rec_in_all + (((size_t)b * HV + h) * DK) * DK;
       float *S_out = rec_out_all + (((size_t)b * HV + h) * DK) * DK;
-      // state thread mapping: col c, rows r0..r0+7
-      const int c = lane & 15;
-      const int rbase = warp * 16 + (lane >> 4) * 8;
       const int col = t * 16 + c;
+      float S[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) S[i] = S_in[(size_t)(rbase + i) * DK + col];
       if (p.q_len[b] == 0) {
         // Empty row: replacement state equals the input state (a no-op when in place).
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          S_out[(size_t)(rbase + i) * DK + col] = S_in[(size_t)(rbase + i) * DK + col];
+        for (int i = 0; i < 8; ++i) S_out[(size_t)(rbase + i) * DK + col] = S[i];
         if (tid < 16) p.core[(size_t)b * HV * DK + h * DK + t * 16 + tid] = tobf(0.f);
         if (tid == 0) p.ssq[((size_t)b * HV + h) * 8 + t] = 0.f;
         continue;
       }
+      const bf16 *cin = conv_in_all + (size_t)b * CH * CW;
       const bf16 *x = p.proj + (size_t)b * p.pstride;
-      // causal conv (width 4) over [conv[1..3], x] + SiLU, rounded as recurrent.py:32-58.
-      // The updated conv window is written after the next grid barrier (conv_state_update), so
-      // the state may be updated in place.
-      auto conv = [&](int ch) -> float {
-        const float h0 = bf(cin[ch * CW + 1]), h1 = bf(cin[ch * CW + 2]), h2 = bf(cin[ch * CW + 3]);
-        const float h3 = bf(ldcg_bf(x + ch));
+      // conv channels: q (tid < 128) or k (tid >= 128) of key head kh; v channel for tid < 16
+      const int chq = tid < DK ? kh * DK + tid : (HK + kh) * DK + (tid - DK);
+      const int chv = (2 * HK + h) * DK + t * 16 + (tid & 15);
+      const uint2 cq = *reinterpret_cast<const uint2 *>(cin + (size_t)chq * CW);
+      const uint2 wq = *reinterpret_cast<const uint2 *>(cw + (size_t)chq * CW);
+      const float xq = bf(ldcg_bf(x + chq));
+      uint2 cv = make_uint2(0, 0), wvv = make_uint2(0, 0);
+      float xv = 0.f;
+      if (tid < 16) {
+        cv = *reinterpret_cast<const uint2 *>(cin + (size_t)chv * CW);
+        wvv = *reinterpret_cast<const uint2 *>(cw + (size_t)chv * CW);
+        xv = bf(ldcg_bf(x + chv));
+      }
+      float gsc = 0.f;
+      if (warp == 0) {
+        if (lane == 0) gsc = bf(ldcg_bf(x + CH + HV * DK + h));           // b
+        else if (lane == 1) gsc = bf(ldcg_bf(x + CH + HV * DK + HV + h));  // a
+        else if (lane == 2) gsc = bf(((const bf16 *)w.dt_bias)[h]);
+        else if (lane == 3) gsc = bf(((const bf16 *)w.a_log)[h]);
+      }
+      // causal conv (width 4) over [conv[1..3], x] + SiLU, rounded as recurrent.py:32-58
+      auto conv = [](uint2 cs, uint2 ws, float xx) -> float {
         float tot = 0.f;
-        tot = fmaf(h0, bf(cw[ch * CW + 0]), tot);
-        tot = fmaf(h1, bf(cw[ch * CW + 1]), tot);
-        tot = fmaf(h2, bf(cw[ch * CW + 2]), tot);
-        tot = fmaf(h3, bf(cw[ch * CW + 3]), tot);
+        tot = fmaf(bf_hi(cs.x), bf_lo(ws.x), tot);
+        tot = fmaf(bf_lo(cs.y), bf_hi(ws.x), tot);
+        tot = fmaf(bf_hi(cs.y), bf_lo(ws.y), tot);
+        tot = fmaf(xx, bf_hi(ws.y), tot);
         const float v = rbf(tot);
         return rbf(v * (1.f / (1.f + expf(-v))));
       };
-      if (tid < 2 * DK) {
-        const int ch = tid < DK ? kh * DK + tid : (HK + kh) * DK + (tid - DK);
-        qk[tid] = conv(ch);
+      const float qkv_val = conv(cq, wq, xq);
+      qk[tid] = qkv_val;
+      if (tid < 16) vv[tid] = conv(cv, wvv, xv);
+      if (warp == 0) {
+        const float bb = __shfl_sync(0xffffffffu, gsc, 0);
+        const float aa = __shfl_sync(0xffffffffu, gsc, 1);
+        const float dt = __shfl_sync(0xffffffffu, gsc, 2);
+        const float al = __shfl_sync(0xffffffffu, gsc, 3);
+        if (lane == 0) {
+          gt[0] = rbf(1.f / (1.f + expf(-bb)));  // beta
+          const float xx = aa + dt;
+          const float sp = xx > 20.f ? xx : log1pf(expf(xx));
+          gt[1] = expf(-expf(al) * sp);          // decay = exp(g)
+        }
       }
-      if (tid < 16) vv[tid] = conv((2 * HK + h) * DK + t * 16 + tid);
-      csync();
-      // L2 norms of q (warps 0-3) and k (warps 4-7)
       {
-        const float x0 = qk[tid];
-        float s = warp_sum(x0 * x0);
-        if (lane == 0) part[warp] = s;
+        const float sq = warp_sum(qkv_val * qkv_val);
+        if (lane == 0) pn[warp] = sq;
       }
       csync();
-      if (tid == 0) {
-        const float sq = part[0] + part[1] + part[2] + part[3];
-        const float sk = part[4] + part[5] + part[6] + part[7];
-        misc[0] = rsqrtf(sq + 1e-6f);
-        misc[1] = rsqrtf(sk + 1e-6f);
-        const float bb = bf(ldcg_bf(x + CH + HV * DK + h));
-        misc[2] = rbf(1.f / (1.f + expf(-bb)));  // beta
-        const float a = bf(ldcg_bf(x + CH + HV * DK + HV + h));
-        const float xx = a + bf(((const bf16 *)w.dt_bias)[h]);
-        const float sp = xx > 20.f ? xx : log1pf(expf(xx));
-        const float g = -expf(bf(((const bf16 *)w.a_log)[h])) * sp;
-        misc[3] = expf(g);  // decay
-      }
-      csync();
-      const float qs = misc[0], ks = misc[1], beta = misc[2], decay = misc[3];
-      const float qscale = p.dk_scale;
-      float S[8], kr[8], qr[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        S[i] = S_in[(size_t)(rbase + i) * DK + col];
-        kr[i] = qk[DK + rbase + i] * ks;
-        qr[i] = qk[rbase + i] * qs * qscale;
-      }
+      const float qs = rsqrtf(pn[0] + pn[1] + pn[2] + pn[3] + 1e-6f);
+      const float ks = rsqrtf(pn[4] + pn[5] + pn[6] + pn[7] + 1e-6f);
+      const float beta = gt[0], decay = gt[1];
+      float kr[8], qr[8];
       float pr = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) { S[i] *= decay; pr = fmaf(S[i], kr[i], pr); }
+      for (int i = 0; i < 8; ++i) {
+        kr[i] = qk[DK + rbase + i] * ks;
+        qr[i] = qk[rbase + i] * qs * p.dk_scale;
+        S[i] *= decay;
+        pr = fmaf(S[i], kr[i], pr);
+      }
       pr += __shfl_xor_sync(0xffffffffu, pr, 16);
-      if (lane < 16) part[warp * 16 + lane] = pr;
+      if (lane < 16) pp[warp * 16 + lane] = pr;
       csync();
       float pred = 0.f;
-      for (int i = 0; i < kWarps; ++i) pred += part[i * 16 + c];
+#pragma unroll
+      for (int i = 0; i < kWarps; ++i) pred += pp[i * 16 + c];
       const float delta_c = (vv[c] - pred) * beta;
-      csync();  // part[] reused below
       float o = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -719,11 +883,12 @@ template <int NB> struct Consumer {
         S_out[(size_t)(rbase + i) * DK + col] = S[i];
       }
       o += __shfl_xor_sync(0xffffffffu, o, 16);
-      if (lane < 16) part[warp * 16 + lane] = o;
+      if (lane < 16) po[warp * 16 + lane] = o;
       csync();
       if (tid < 16) {
         float out = 0.f;
-        for (int i = 0; i < kWarps; ++i) out += part[i * 16 + tid];
+#pragma unroll
+        for (int i = 0; i < kWarps; ++i) out += po[i * 16 + tid];
         const float ob = rbf(out);
         p.core[(size_t)b * HV * DK + h * DK + t * 16 + tid] = tobf(ob);
         float sq = ob * ob;
@@ -731,7 +896,6 @@ template <int NB> struct Consumer {
         for (int o2 = 8; o2; o2 >>= 1) sq += __shfl_xor_sync(0x0000ffffu, sq, o2);
         if (tid == 0) p.ssq[((size_t)b * HV + h) * 8 + t] = sq;
       }
-      csync();
     }
   }
 
@@ -998,7 +1162,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       Producer pr(p, hdr, ring);
       const uint64_t t_start = globaltimer();
       walk_step(p, pr);
-      if (p.trace) p.trace[(size_t)blockIdx.x * kTraceStride + 2 * kTraceStages + 3] = globaltimer() - t_start;
+      if (p.trace) {
+        p.trace[(size_t)blockIdx.x * kTraceStride + 3 * kTraceStages + 3] = globaltimer() - t_start;
+        p.trace[(size_t)blockIdx.x * kTraceStride + 3 * kTraceStages + 4] = pr.empty_wait;
+        p.trace[(size_t)blockIdx.x * kTraceStride + 3 * kTraceStages + 5] = (unsigned long long)pr.issued;
+      }
       // Drain: never leave with bulk copies in flight into this CTA's shared memory. Phases of
       // one slot complete in order, so waiting for the last copy issued into each slot suffices.
       for (int k = max(0, pr.issued - p.nslots); k < pr.issued; ++k) {

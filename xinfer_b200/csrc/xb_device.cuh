@@ -35,6 +35,24 @@ __device__ __forceinline__ void unpack8(const uint4 &v, float (&f)[8]) {
   f[6] = bf_lo(v.w); f[7] = bf_hi(v.w);
 }
 
+// acc + sum_{e=0..7} w[e] * x[e] for eight bf16 pairs, accumulated in order e = 0..7 with one
+// rounding per step: fma with bf16 multiplicands and an fp32 addend/result, so no unpacking.
+__device__ __forceinline__ float dot8_bf16(const uint4 &w, const uint4 &x, float acc) {
+  asm("{\n\t"
+      ".reg .b16 w0, w1, w2, w3, w4, w5, w6, w7, x0, x1, x2, x3, x4, x5, x6, x7;\n\t"
+      "mov.b32 {w0, w1}, %1;\n\tmov.b32 {w2, w3}, %2;\n\t"
+      "mov.b32 {w4, w5}, %3;\n\tmov.b32 {w6, w7}, %4;\n\t"
+      "mov.b32 {x0, x1}, %5;\n\tmov.b32 {x2, x3}, %6;\n\t"
+      "mov.b32 {x4, x5}, %7;\n\tmov.b32 {x6, x7}, %8;\n\t"
+      "fma.rn.f32.bf16 %0, w0, x0, %0;\n\tfma.rn.f32.bf16 %0, w1, x1, %0;\n\t"
+      "fma.rn.f32.bf16 %0, w2, x2, %0;\n\tfma.rn.f32.bf16 %0, w3, x3, %0;\n\t"
+      "fma.rn.f32.bf16 %0, w4, x4, %0;\n\tfma.rn.f32.bf16 %0, w5, x5, %0;\n\t"
+      "fma.rn.f32.bf16 %0, w6, x6, %0;\n\tfma.rn.f32.bf16 %0, w7, x7, %0;\n\t}"
+      : "+f"(acc)
+      : "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w), "r"(x.x), "r"(x.y), "r"(x.z), "r"(x.w));
+  return acc;
+}
+
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);  // .x = a (low), .y = b (high)
   return *reinterpret_cast<uint32_t *>(&h);
@@ -73,6 +91,9 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
 }
 __device__ __forceinline__ void st_release(unsigned *p, unsigned v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ unsigned ld_volatile(const unsigned *p) {
   return *reinterpret_cast<const volatile unsigned *>(p);
