@@ -39,17 +39,21 @@ constexpr int kThreads = kCT + 32;        // + producer warp
 constexpr int kSlot = 32768;              // ring slot bytes
 constexpr int kMaxSlots = 8;
 constexpr int kHdrBytes = 512;
+constexpr int kResRows = 32;                           // residual rows a CTA owns (<= 32)
+constexpr int kResBytes = XB_MAX_BATCH * kResRows * 4;
 constexpr int kRedFloats = 1024;
-constexpr int kUOffset = kHdrBytes + kRedFloats * 4;  // 4608, 128-aligned
+constexpr int kUOffset = kHdrBytes + kResBytes + kRedFloats * 4;  // 5632, 128-aligned
 constexpr int kSmemLimit = 232448;                     // 227 KB opt-in per CTA
 // layout of the per-CTA float scratch `red` during GEMV stages
 constexpr int RED_RESID = 64;   // [NB][rows of this CTA] residual rows (<= 256)
 constexpr int RED_PART = 512;   // [2][kWarps][2][NB][2] split-K partials
 
 // control words in the workspace (each on its own 128-byte line)
-enum { CTL_ERR = 64, CTL_DONE = 96, CTL_BAR = 128, CTL_WORDS = 128 + 8 * 32 };
+// Words [0, CTL_WORDS) are cleared whenever a workspace is reset; the launch epoch (which
+// stamps every inter-stage value with a tag) lives after them and only ever advances.
+enum { CTL_ERR = 64, CTL_DONE = 96, CTL_WORDS = 128, CTL_EPOCH = 128, CTL_TOTAL = 160 };
 // device error codes
-enum { DERR_BARRIER = 1, DERR_RING_FULL = 2, DERR_RING_EMPTY = 3, DERR_TOKEN = 4, DERR_DRAIN = 5 };
+enum { DERR_WAIT = 1, DERR_RING_FULL = 2, DERR_RING_EMPTY = 3, DERR_TOKEN = 4, DERR_DRAIN = 5 };
 
 enum Stage {
   ST_IN_DELTA = 0, ST_OUT_DELTA, ST_QKV, ST_O, ST_GATEUP, ST_DOWN, ST_LMHEAD
@@ -71,8 +75,11 @@ struct StepParams {
   bf16 *logits;
   int64_t *tokens;
   unsigned *ctrl;
-  bf16 *h, *proj, *core, *att_out, *act;
-  float *ssq, *att_o, *att_ml, *am_v;
+  // inter-stage buffers of tagged words: (bf16 bits | tag << 16) or {fp32 bits, tag}
+  unsigned *h, *proj, *core, *att_out, *act;
+  uint2 *ssq, *att_o;
+  uint4 *att_ml;
+  float *am_v;
   int *am_i;
   // Optional stage trace (see xb_debug_trace): per CTA kTraceStages x {arrive, release} stamps
   // of %globaltimer plus ring-wait totals; NULL when tracing is off.
@@ -86,6 +93,7 @@ struct SmemHdr {
   uint64_t empty[kMaxSlots];
   int abort;
   int is_last;
+  unsigned epoch;
 };
 static_assert(sizeof(SmemHdr) <= kHdrBytes, "header");
 
@@ -203,12 +211,14 @@ struct Producer {
     while (!mbar_try_wait(&hdr->empty[slot], phase ^ 1u) ||
            (issued >= p.nslots && !mbar_try_wait(&hdr->full[slot], phase ^ 1u))) {
       if ((++spins & 63u) == 0) {
-        if (ld_volatile(p.ctrl + CTL_ERR)) return false;
         const uint64_t t = globaltimer();
         if (t0 == 0) t0 = t;
-        else if (t - t0 > 2 * kWaitLimitNs) {
-          atomicCAS(p.ctrl + CTL_ERR, 0u, (unsigned)DERR_RING_EMPTY);
-          return false;
+        else if (t - t0 > kSlowWaitNs) {
+          if (ld_volatile(p.ctrl + CTL_ERR)) return false;
+          if (t - t0 > 2 * kWaitLimitNs) {
+            atomicCAS(p.ctrl + CTL_ERR, 0u, (unsigned)DERR_RING_EMPTY);
+            return false;
+          }
         }
       }
     }
@@ -252,38 +262,155 @@ struct Producer {
   __device__ void comb(int) {}
 };
 
+
+// One warp's share of a GEMV tile: rows A and B (and, for gate/up tiles, their up rows) dotted
+// with the NB activation rows over K chunks [cb, ce), reduced over the warp. Returns, for lane
+// b (< NB) the row-A result of batch row b and for lane 16 + b the row-B result (.y = up row).
+// Kept out of line so that its code is generated independently of the surrounding megakernel.
+template <bool PAIRED, int NB>
+__device__ __forceinline__ float2 gemv_pair(const uint4 *__restrict__ wA, const uint4 *__restrict__ wB,
+                                         const uint4 *__restrict__ uA, const uint4 *__restrict__ uB,
+                                         const uint4 *__restrict__ act4, int n8, int cb, int ce) {
+  const int lane = threadIdx.x & 31;
+  float a0[NB], c0[NB], a1[NB], c1[NB];
+#pragma unroll
+  for (int b = 0; b < NB; ++b) { a0[b] = c0[b] = a1[b] = c1[b] = 0.f; }
+  if (PAIRED) {
+#pragma unroll 2
+    for (int j = cb + lane; j < ce; j += 32) {
+      const uint4 wa = wA[j], wb = wB[j], ua = uA[j], ub = uB[j];
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        const uint4 x = act4[b * n8 + j];
+        a0[b] = dot8_bf16(wa, x, a0[b]);
+        c0[b] = dot8_bf16(wb, x, c0[b]);
+        a1[b] = dot8_bf16(ua, x, a1[b]);
+        c1[b] = dot8_bf16(ub, x, c1[b]);
+      }
+    }
+  } else {
+#pragma unroll 4
+    for (int j = cb + lane; j < ce; j += 32) {
+      const uint4 wa = wA[j], wb = wB[j];
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        const uint4 x = act4[b * n8 + j];
+        a0[b] = dot8_bf16(wa, x, a0[b]);
+        c0[b] = dot8_bf16(wb, x, c0[b]);
+      }
+    }
+  }
+  const int bsel = lane & 15;
+  const bool second = lane >= 16;
+  float2 r = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    const float sa = warp_sum(a0[b]), sc = warp_sum(c0[b]);
+    float ta = 0.f, tc = 0.f;
+    if (PAIRED) { ta = warp_sum(a1[b]); tc = warp_sum(c1[b]); }
+    if (bsel == b) r = second ? make_float2(sc, tc) : make_float2(sa, ta);
+  }
+  return r;
+}
+
+
+// ---- waits (free functions: the consumer object must never have its address taken, so that
+// its state stays in registers) -------------------------------------------------------------
+// True when a wait must end: this CTA aborted, or (only after kSlowWaitNs of waiting, so that the
+// hot hand-offs never pay for a global load) the grid reported an error or the limit passed.
+__device__ __forceinline__ bool wait_give_up(volatile int *abort_flag, unsigned *ctrl, uint64_t &t0) {
+  if (*abort_flag) return true;
+  const uint64_t t = globaltimer();
+  if (t0 == 0) { t0 = t; return false; }
+  if (t - t0 < kSlowWaitNs) return false;
+  if (ld_volatile(ctrl + CTL_ERR)) { *abort_flag = 1; return true; }
+  if (t - t0 > kWaitLimitNs) {
+    atomicCAS(ctrl + CTL_ERR, 0u, (unsigned)DERR_WAIT);
+    *abort_flag = 1;
+    return true;
+  }
+  return false;
+}
+__device__ __noinline__ uint4 repoll4(const unsigned *w, unsigned tg, volatile int *abort_flag,
+                                      unsigned *ctrl) {
+  uint4 v;
+  uint64_t t0 = 0;
+  for (unsigned spins = 1;; ++spins) {
+    v = ld_poll_u4(w);
+    if (tag4_ok(v, tg)) break;
+    if ((spins & 15u) == 0 && wait_give_up(abort_flag, ctrl, t0)) break;
+  }
+  return v;
+}
+__device__ __noinline__ unsigned repoll1(const unsigned *w, unsigned tg, volatile int *abort_flag,
+                                         unsigned *ctrl) {
+  unsigned v;
+  uint64_t t0 = 0;
+  for (unsigned spins = 1;; ++spins) {
+    v = ld_poll_u32(w);
+    if ((v >> 16) == tg) break;
+    if ((spins & 15u) == 0 && wait_give_up(abort_flag, ctrl, t0)) break;
+  }
+  return v;
+}
+__device__ __noinline__ uint4 repoll2f(const uint2 *w, unsigned tg, volatile int *abort_flag,
+                                       unsigned *ctrl) {
+  uint4 v;
+  uint64_t t0 = 0;
+  for (unsigned spins = 1;; ++spins) {
+    v = ld_poll_u4(w);
+    if (v.y == tg && v.w == tg) break;
+    if ((spins & 15u) == 0 && wait_give_up(abort_flag, ctrl, t0)) break;
+  }
+  return v;
+}
+__device__ __noinline__ float repoll1f(const uint2 *w, unsigned tg, volatile int *abort_flag,
+                                       unsigned *ctrl) {
+  uint2 v;
+  uint64_t t0 = 0;
+  for (unsigned spins = 1;; ++spins) {
+    v = ld_poll_u2(w);
+    if (v.y == tg) break;
+    if ((spins & 15u) == 0 && wait_give_up(abort_flag, ctrl, t0)) break;
+  }
+  return __uint_as_float(v.x);
+}
+
 // ------------------------------------------------------------------------------------------
 // Consumer role
 // ------------------------------------------------------------------------------------------
 template <int NB> struct Consumer {
   const StepParams &p;
   SmemHdr *hdr;
-  float *red;     // kRedFloats
+  float *red;     // kRedFloats scratch, reused stage by stage
+  float *hres;    // [NB][kResRows] this CTA's rows of the residual stream, kept across stages
   char *U;        // union region: GEMV activations / attention scratch
   char *ring;
   int tid, warp, lane;
   int slot = 0;
   unsigned phase = 0;
-  bool first = true;      // first stage of the step needs no barrier
-  bool h_ready = false;   // residual stream in p.h (false: still the embedding rows)
+  bool h_ready = false;   // residual stream published (false: still the embedding rows)
   int sidx = 0;           // stage counter (trace)
-  int nbar = 0;           // grid barriers passed in this launch
-  unsigned long long full_wait = 0;  // ns spent waiting for ring slots (trace, tid 0)
-  // running argmax for the lm_head stage (lane b keeps batch row b)
+  unsigned epoch;
+  unsigned long long full_wait = 0;  // ns waiting for ring slots (trace, tid 0)
+  unsigned long long poll_wait = 0;  // ns waiting for tagged inputs (trace, tid 0)
+  // running argmax for the lm_head stage (lane b / 16 + b keeps batch row b)
   float am_v = -INFINITY;
   int am_i = 0x7fffffff;
 
-  __device__ Consumer(const StepParams &p_, SmemHdr *h, float *r, char *u, char *rg)
-      : p(p_), hdr(h), red(r), U(u), ring(rg) {
+  __device__ Consumer(const StepParams &p_, SmemHdr *h, float *r, float *hr, char *u, char *rg)
+      : p(p_), hdr(h), red(r), hres(hr), U(u), ring(rg) {
     tid = threadIdx.x;
     warp = tid >> 5;
     lane = tid & 31;
+    epoch = hdr->epoch;
   }
 
   __device__ __forceinline__ void csync() { named_sync<kCT>(1); }
+  __device__ __forceinline__ unsigned tag(int l, int k) const { return tag_of(epoch, l, k); }
 
   // Abort rules: every consumer thread always executes the same sequence of named barriers.
-  // An abort (device error word set anywhere in the grid) only skips waits and GEMV tiles.
+  // An abort (device error word set anywhere in the grid) only makes waits give up.
   __device__ __forceinline__ bool aborted() const {
     return *reinterpret_cast<volatile int *>(&hdr->abort) != 0;
   }
@@ -291,52 +418,36 @@ template <int NB> struct Consumer {
     atomicCAS(p.ctrl + CTL_ERR, 0u, code);
     *reinterpret_cast<volatile int *>(&hdr->abort) = 1;
   }
+  __device__ __forceinline__ volatile int *abort_flag() const {
+    return reinterpret_cast<volatile int *>(&hdr->abort);
+  }
+  __device__ __forceinline__ bool give_up(uint64_t &t0) const {
+    return wait_give_up(abort_flag(), p.ctrl, t0);
+  }
 
-  // Grid barrier: one release-reduction per CTA onto one of eight counters (spreading the
-  // atomic traffic over eight L2 lines), then lanes 0-7 of warp 0 poll the eight counters with
-  // acquire loads until their sum reaches (barriers so far) x (CTAs). The counters are monotonic
-  // within a launch and reset by the last CTA to finish the step.
-  __device__ void grid_sync() {
-    csync();
-    ++nbar;
-    if (warp == 0 && !aborted()) {
-      unsigned *ctrl = p.ctrl;
-      if (lane == 0) red_release_add(ctrl + CTL_BAR + (blockIdx.x & 7) * 32, 1u);
-      const unsigned target = (unsigned)nbar * (unsigned)p.ncta;
-      const uint64_t t0 = globaltimer();
-      unsigned spins = 0;
-      for (;;) {
-        unsigned v = lane < 8 ? ld_acquire(ctrl + CTL_BAR + lane * 32) : 0u;
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        v += __shfl_xor_sync(0xffffffffu, v, 4);
-        if (__shfl_sync(0xffffffffu, v, 0) >= target) break;
-        if ((++spins & 127u) == 0) {
-          int stop = 0;
-          if (lane == 0) {
-            if (ld_volatile(ctrl + CTL_ERR)) stop = 1;
-            else if (globaltimer() - t0 > kWaitLimitNs) {
-              atomicCAS(ctrl + CTL_ERR, 0u, (unsigned)DERR_BARRIER);
-              stop = 1;
-            }
-          }
-          if (__shfl_sync(0xffffffffu, stop, 0)) {
-            if (lane == 0) *reinterpret_cast<volatile int *>(&hdr->abort) = 1;
-            break;
-          }
-        }
-      }
-    }
-    csync();
+  // ---- tagged inputs -----------------------------------------------------------------------
+  // Callers load first (plain L2 loads, all issued together) and only fall into the
+  // non-inlined slow paths for words whose tag is not there yet.
+  __device__ __forceinline__ uint4 poll4(const unsigned *w, unsigned tg) const {
+    const uint4 v = ldcg_u4(w);
+    return tag4_ok(v, tg) ? v : repoll4(w, tg, abort_flag(), p.ctrl);
+  }
+  __device__ __forceinline__ uint4 check4(const unsigned *w, uint4 v, unsigned tg) const {
+    return tag4_ok(v, tg) ? v : repoll4(w, tg, abort_flag(), p.ctrl);
+  }
+  __device__ __forceinline__ unsigned poll1(const unsigned *w, unsigned tg) const {
+    const unsigned v = ld_poll_u32(w);
+    return (v >> 16) == tg ? v : repoll1(w, tg, abort_flag(), p.ctrl);
+  }
+  __device__ __forceinline__ uint4 poll2f(const uint2 *w, unsigned tg) const {
+    const uint4 v = ldcg_u4(w);
+    return (v.y == tg && v.w == tg) ? v : repoll2f(w, tg, abort_flag(), p.ctrl);
   }
 
   __device__ void stage_begin() {
     unsigned long long *tr = p.trace ? p.trace + (size_t)blockIdx.x * kTraceStride : nullptr;
     const int si = sidx < kTraceStages ? sidx : kTraceStages - 1;
-    if (tr && tid == 0) tr[3 * si] = globaltimer();
-    if (first) first = false;
-    else grid_sync();
-    if (tr && tid == 0) tr[3 * si + 1] = tr[3 * si + 2] = globaltimer();
+    if (tr && tid == 0) tr[3 * si] = tr[3 * si + 1] = tr[3 * si + 2] = globaltimer();
     ++sidx;
   }
   __device__ void trace_mark() {  // end of a GEMV stage's prologue
@@ -351,6 +462,7 @@ template <int NB> struct Consumer {
       tr[3 * kTraceStages] = globaltimer();
       tr[3 * kTraceStages + 1] = full_wait;
       tr[3 * kTraceStages + 2] = (unsigned long long)sidx;
+      tr[3 * kTraceStages + 6] = poll_wait;
     }
   }
 
@@ -360,19 +472,7 @@ template <int NB> struct Consumer {
     unsigned spins = 0;
     const uint64_t tw = (p.trace && tid == 0) ? globaltimer() : 0;
     while (!mbar_try_wait(&hdr->full[slot], phase)) {
-      if ((++spins & 63u) == 0) {
-        if (aborted()) return nullptr;
-        if (ld_volatile(p.ctrl + CTL_ERR)) {
-          *reinterpret_cast<volatile int *>(&hdr->abort) = 1;
-          return nullptr;
-        }
-        const uint64_t t = globaltimer();
-        if (t0 == 0) t0 = t;
-        else if (t - t0 > kWaitLimitNs) {
-          set_abort(DERR_RING_FULL);
-          return nullptr;
-        }
-      }
+      if ((++spins & 63u) == 0 && give_up(t0)) return nullptr;
     }
     if (p.trace && tid == 0) full_wait += globaltimer() - tw;
     return ring + (size_t)slot * kSlot;
@@ -383,44 +483,58 @@ template <int NB> struct Consumer {
     if (++slot == p.nslots) { slot = 0; phase ^= 1u; }
   }
 
-  // 16 bytes (8 bf16) of residual-stream row b at element e (embedding row before the first
-  // residual update, which is read-only; afterwards the stream written by other CTAs).
-  __device__ __forceinline__ uint4 hchunk(int b, int e) const {
-    if (!h_ready) return ldnc_u4(p.embed + (size_t)token_id(p, b) * p.H + e);
-    return ldcg_u4(p.h + (size_t)b * p.H + e);
-  }
-  __device__ __forceinline__ float hval(int b, int e) const {
-    if (!h_ready) return bf(p.embed[(size_t)token_id(p, b) * p.H + e]);
-    return bf(ldcg_bf(p.h + (size_t)b * p.H + e));
-  }
-
-  // Residual rows [lo, hi) of this CTA, read before the tile loop (RESID epilogues).
-  __device__ __forceinline__ float resid_load(int lo, int hi) const {
-    const int n = hi - lo;
-    const int b = tid / max(n, 1), r = tid - b * max(n, 1);
-    return (n > 0 && b < NB && b < p.B) ? hval(b, lo + r) : 0.f;
-  }
-  __device__ __forceinline__ void resid_store(float v, int lo, int hi) {
-    const int n = hi - lo;
-    if (n > 0 && tid < NB * n) red[RED_RESID + tid] = v;
+  // 16 bytes (8 bf16) of residual-stream row b at element e: the embedding row before layer 0's
+  // first residual update, afterwards the tagged stream written by the RESID epilogues.
+  __device__ __forceinline__ uint4 pack_words(const uint4 &a, const uint4 &c) {
+    return make_uint4((a.x & 0xffffu) | (a.y << 16), (a.z & 0xffffu) | (a.w << 16),
+                      (c.x & 0xffffu) | (c.y << 16), (c.z & 0xffffu) | (c.w << 16));
   }
 
   // RMSNorm of the residual stream into the activation buffer (bf16 [NB][H]).
   //  Qwen3   : w * bf16(x * rsqrt(mean(x^2) + eps))        (HF Qwen3RMSNorm)
   //  Qwen3.5 : bf16(x * rsqrt(mean(x^2) + eps) * (1 + w))   (HF Qwen3_5RMSNorm)
-  // All loads are issued before any use: one round trip to L2 per stage.
-  __device__ void norm_prologue(const bf16 *w) {
+  __device__ void norm_prologue(const bf16 *w, unsigned tg) {
     uint4 *act = reinterpret_cast<uint4 *>(U);
     const int H = p.H, nc = H / 8;
     constexpr int MAXC = 2;  // H <= 2 * 256 * 8
     uint4 xv[NB][MAXC], wv[MAXC];
+    if (!h_ready) {
 #pragma unroll
-    for (int i = 0; i < MAXC; ++i) {
-      const int c = tid + i * kCT;
-      wv[i] = c < nc ? ldnc_u4(w + c * 8) : make_uint4(0, 0, 0, 0);
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = tid + i * kCT;
+        wv[i] = c < nc ? ldnc_u4(w + c * 8) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-      for (int b = 0; b < NB; ++b)
-        xv[b][i] = (c < nc && b < p.B) ? hchunk(b, c * 8) : make_uint4(0, 0, 0, 0);
+        for (int b = 0; b < NB; ++b)
+          xv[b][i] = (c < nc && b < p.B) ? ldnc_u4(p.embed + (size_t)token_id(p, b) * H + c * 8)
+                                          : make_uint4(0, 0, 0, 0);
+      }
+    } else {
+      uint4 lo4[NB][MAXC], hi4[NB][MAXC];
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = tid + i * kCT;
+        wv[i] = c < nc ? ldnc_u4(w + c * 8) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          const bool ok = c < nc && b < p.B;
+          lo4[b][i] = ok ? ldcg_u4(p.h + (size_t)b * H + c * 8) : make_uint4(0, 0, 0, 0);
+          hi4[b][i] = ok ? ldcg_u4(p.h + (size_t)b * H + c * 8 + 4) : make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = tid + i * kCT;
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          if (c < nc && b < p.B) {
+            const uint4 a = check4(p.h + (size_t)b * H + c * 8, lo4[b][i], tg);
+            const uint4 d = check4(p.h + (size_t)b * H + c * 8 + 4, hi4[b][i], tg);
+            xv[b][i] = pack_words(a, d);
+          } else {
+            xv[b][i] = make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
     }
     float ss[NB];
 #pragma unroll
@@ -462,23 +576,29 @@ template <int NB> struct Consumer {
     }
   }
 
-  // Copy a bf16 scratch vector [B][K] (stride ld) produced this launch into the activations.
-  __device__ void copy_prologue(const bf16 *src, int K, int ld) {
-    uint4 *act = reinterpret_cast<uint4 *>(U);
-    const int nc = K / 8;
-    constexpr int MAXC = 5;  // K <= 5 * 256 * 8
+  // Tagged bf16 vector [B][K] (row stride ld words) into the activations.
+  __device__ void copy_prologue(const unsigned *src, int K, int ld, unsigned tg) {
+    uint2 *act = reinterpret_cast<uint2 *>(U);  // 4 bf16 per uint2
+    const int nq = K / 4;
+    constexpr int MAXC = 10;  // K <= 10 * 256 * 4
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
       uint4 v[MAXC];
 #pragma unroll
       for (int i = 0; i < MAXC; ++i) {
         const int c = tid + i * kCT;
-        v[i] = (c < nc && b < p.B) ? ldcg_u4(src + (size_t)b * ld + c * 8) : make_uint4(0, 0, 0, 0);
+        v[i] = (c < nq && b < p.B) ? ldcg_u4(src + (size_t)b * ld + c * 4) : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
       for (int i = 0; i < MAXC; ++i) {
         const int c = tid + i * kCT;
-        if (c < nc) act[b * nc + c] = v[i];
+        if (c >= nq) continue;
+        uint2 o = make_uint2(0, 0);
+        if (b < p.B) {
+          const uint4 q = check4(src + (size_t)b * ld + c * 4, v[i], tg);
+          o = make_uint2((q.x & 0xffffu) | (q.y << 16), (q.z & 0xffffu) | (q.w << 16));
+        }
+        act[b * nq + c] = o;
       }
     }
   }
@@ -486,54 +606,52 @@ template <int NB> struct Consumer {
   // Gated RMSNorm of the DeltaNet core output (HF Qwen3_5RMSNormGated, as called in
   // compiler/qwen35/adapters/delta.py:46-47): y = bf16( bf16(w * bf16(x * r)) * silu(z) ).
   // Each thread derives its head's 1/rms from the eight per-tile partial sums itself.
-  __device__ void gated_norm_prologue(const bf16 *w) {
-    uint4 *act = reinterpret_cast<uint4 *>(U);
-    const int K = p.HV * p.DK, nc = K / 8, DK = p.DK;
+  __device__ void gated_norm_prologue(const bf16 *w, unsigned tg) {
+    uint2 *act = reinterpret_cast<uint2 *>(U);
+    const int K = p.HV * p.DK, nq = K / 4, DK = p.DK;
     const int zoff = 2 * p.HK * p.DK + p.HV * p.DK;
-    constexpr int MAXC = 2;  // K <= 4096
+    constexpr int MAXC = 4;  // K <= 4 * 256 * 4
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
-      uint4 xv[MAXC], zv[MAXC], wv[MAXC];
-      float part[MAXC][8];
 #pragma unroll
       for (int i = 0; i < MAXC; ++i) {
         const int c = tid + i * kCT;
-        const bool ok = c < nc && b < p.B;
-        xv[i] = ok ? ldcg_u4(p.core + (size_t)b * K + c * 8) : make_uint4(0, 0, 0, 0);
-        zv[i] = ok ? ldcg_u4(p.proj + (size_t)b * p.pstride + zoff + c * 8) : make_uint4(0, 0, 0, 0);
-        wv[i] = c < nc ? ldnc_u4(w + (c * 8) % DK) : make_uint4(0, 0, 0, 0);
-        const int h = (c * 8) / DK;
+        if (c >= nq) continue;
+        uint2 o = make_uint2(0, 0);
+        if (b < p.B) {
+          const uint4 xv = poll4(p.core + (size_t)b * K + c * 4, tg);
+          const uint4 zv = poll4(p.proj + (size_t)b * p.pstride + zoff + c * 4, tg);
+          const uint2 wv = *reinterpret_cast<const uint2 *>(w + (c * 4) % DK);
+          const int h = (c * 4) / DK;
+          const uint2 *ps = p.ssq + ((size_t)b * p.HV + h) * 8;
+          float tot = 0.f;
 #pragma unroll
-        for (int t = 0; t < 8; ++t)
-          part[i][t] = ok ? ldcg_f(p.ssq + ((size_t)b * p.HV + h) * 8 + t) : 0.f;
-      }
+          for (int t = 0; t < 8; t += 2) {
+            const uint4 q = poll2f(ps + t, tg);
+            tot += __uint_as_float(q.x);
+            tot += __uint_as_float(q.z);
+          }
+          const float r = rsqrtf(tot / (float)DK + p.eps);
+          const float x[4] = {bf_lo(xv.x), bf_lo(xv.y), bf_lo(xv.z), bf_lo(xv.w)};
+          const float z[4] = {bf_lo(zv.x), bf_lo(zv.y), bf_lo(zv.z), bf_lo(zv.w)};
+          const float wf[4] = {bf_lo(wv.x), bf_hi(wv.x), bf_lo(wv.y), bf_hi(wv.y)};
+          float y[4];
 #pragma unroll
-      for (int i = 0; i < MAXC; ++i) {
-        const int c = tid + i * kCT;
-        if (c >= nc) continue;
-        float tot = 0.f;
-#pragma unroll
-        for (int t = 0; t < 8; ++t) tot += part[i][t];
-        const float r = rsqrtf(tot / (float)DK + p.eps);
-        float x[8], z[8], wf[8], y[8];
-        unpack8(xv[i], x);
-        unpack8(zv[i], z);
-        unpack8(wv[i], wf);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float n = rbf(wf[e] * rbf(x[e] * r));
-          y[e] = (b < p.B) ? n * (z[e] / (1.f + expf(-z[e]))) : 0.f;
+          for (int e = 0; e < 4; ++e) {
+            const float n = rbf(wf[e] * rbf(x[e] * r));
+            y[e] = n * (z[e] / (1.f + expf(-z[e])));
+          }
+          o = make_uint2(pack2(y[0], y[1]), pack2(y[2], y[3]));
         }
-        act[b * nc + c] = make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]),
-                                     pack2(y[6], y[7]));
+        act[b * nq + c] = o;
       }
     }
   }
 
   // Next conv window per channel: [conv[1], conv[2], conv[3], x] for active rows, unchanged for
-  // empty rows (recurrent.py:43-52). Runs after the barrier that ends the DeltaNet stage, when
-  // no CTA reads the old window any more; each element is read before it is overwritten.
-  __device__ void conv_state_update(int l) {
+  // empty rows (recurrent.py:43-52). Runs in the out_proj stage after its prologue has seen
+  // every head's core output, i.e. after every DeltaNet item has read the old windows.
+  __device__ void conv_state_update(int l, unsigned tg) {
     const int CH = (2 * p.HK + p.HV) * p.DK;
     const uint2 *cin = reinterpret_cast<const uint2 *>(p.sa[l]);
     uint2 *cout = reinterpret_cast<uint2 *>(p.sc[l]);
@@ -544,11 +662,20 @@ template <int NB> struct Consumer {
       const uint2 old = cin[i];
       uint2 nw = old;
       if (p.q_len[b] > 0) {
-        const bf16 xb = ldcg_bf(p.proj + (size_t)b * p.pstride + ch);
+        const unsigned xw = poll1(p.proj + (size_t)b * p.pstride + ch, tg);
         nw.x = (old.x >> 16) | (old.y << 16);
-        nw.y = (old.y >> 16) | ((uint32_t)__bfloat16_as_ushort(xb) << 16);
+        nw.y = (old.y >> 16) | ((xw & 0xffffu) << 16);
       }
       cout[i] = nw;
+    }
+  }
+
+  // This CTA's residual rows from the embedding (before layer 0's first residual update).
+  __device__ void hres_from_embedding(int lo, int hi) {
+    const int n = hi - lo;
+    for (int i = tid; i < NB * n; i += kCT) {
+      const int b = i / n, r = i % n;
+      hres[b * kResRows + r] = b < p.B ? bf(p.embed[(size_t)token_id(p, b) * p.H + lo + r]) : 0.f;
     }
   }
 
@@ -557,44 +684,72 @@ template <int NB> struct Consumer {
   // four), over all of K or, when the tile has fewer than 16 rows, over 1/S of K with the S
   // partial sums combined through shared memory. Lanes 0..NB-1 run the epilogue of the first
   // row for batch rows 0..NB-1, lanes 16..16+NB-1 that of the second row.
-  __device__ void gemv(int l, int stage) {
+  __device__ __forceinline__ void gemv(int l, int stage) {
     stage_begin();
     const Gemv g = make_gemv(p, l, stage);
     const XbLayerWeights *w = (stage == ST_LMHEAD) ? nullptr : &p.layers[l];
     int lo, hi;
     cta_range(g.N, blockIdx.x, p.ncta, lo, hi);
     int epi = EPI_STORE;
+    unsigned otag = 0;  // tag of this stage's outputs
     switch (stage) {
     case ST_IN_DELTA:
-    case ST_QKV: norm_prologue((const bf16 *)w->input_norm); break;
-    case ST_OUT_DELTA: {
-      const float rv = resid_load(lo, hi);
-      conv_state_update(l);
-      gated_norm_prologue((const bf16 *)w->gnorm);
-      resid_store(rv, lo, hi);
-      epi = EPI_RESID;
+    case ST_QKV:
+      norm_prologue((const bf16 *)w->input_norm, l > 0 ? tag(l - 1, 1) : 0u);
+      otag = tag(l, 0);
       break;
-    }
-    case ST_O: {
-      const float rv = resid_load(lo, hi);
-      copy_prologue(p.att_out, g.K, p.HQ * p.D);
-      resid_store(rv, lo, hi);
+    case ST_OUT_DELTA:
+      if (!h_ready) hres_from_embedding(lo, hi);
+      gated_norm_prologue((const bf16 *)w->gnorm, tag(l, 0));
       epi = EPI_RESID;
+      otag = tag(l, 0);
       break;
-    }
-    case ST_GATEUP: norm_prologue((const bf16 *)w->post_norm); epi = EPI_GATEUP; break;
-    case ST_DOWN: {
-      const float rv = resid_load(lo, hi);
-      copy_prologue(p.act, g.K, p.I);
-      resid_store(rv, lo, hi);
+    case ST_O:
+      if (!h_ready) hres_from_embedding(lo, hi);
+      copy_prologue(p.att_out, g.K, p.HQ * p.D, tag(l, 0));
       epi = EPI_RESID;
+      otag = tag(l, 0);
       break;
-    }
-    case ST_LMHEAD: norm_prologue(p.final_norm); epi = EPI_LOGITS; break;
+    case ST_GATEUP:
+      norm_prologue((const bf16 *)w->post_norm, tag(l, 0));
+      epi = EPI_GATEUP;
+      otag = tag(l, 0);
+      break;
+    case ST_DOWN:
+      copy_prologue(p.act, g.K, p.I, tag(l, 0));
+      epi = EPI_RESID;
+      otag = tag(l, 1);
+      break;
+    case ST_LMHEAD:
+      norm_prologue(p.final_norm, tag(p.L - 1, 1));
+      epi = EPI_LOGITS;
+      break;
     }
     csync();
+    // The conv windows may be updated in place only once no DeltaNet item of this layer can
+    // still read them: after the csync above, this CTA has observed every head's core output,
+    // which each item writes after its last read of the old window.
+    if (stage == ST_OUT_DELTA) conv_state_update(l, tag(l, 0));
     trace_mark();
-    const bf16 *act = reinterpret_cast<const bf16 *>(U);
+    switch (epi) {
+    case EPI_STORE: tile_loop<false, EPI_STORE>(g, lo, hi, otag); break;
+    case EPI_RESID: tile_loop<false, EPI_RESID>(g, lo, hi, otag); break;
+    case EPI_GATEUP: tile_loop<true, EPI_GATEUP>(g, lo, hi, otag); break;
+    default: tile_loop<false, EPI_LOGITS>(g, lo, hi, otag); break;
+    }
+    if (epi == EPI_RESID) h_ready = true;
+    if (epi == EPI_LOGITS) {
+      if (p.trace && tid == 0) p.trace[(size_t)blockIdx.x * kTraceStride + 3 * kTraceStages + 7] = globaltimer();
+      argmax_finish();
+    }
+  }
+
+  // Tiles of this CTA's rows [lo, hi) as they arrive in the ring. Full tiles with at least 16
+  // rows take the fast path (one pair of rows per warp per pass, all of K); smaller tiles split K
+  // over S warps per pair and combine the partial sums in shared memory.
+  template <bool PAIRED, int EPI>
+  __device__ __forceinline__ void tile_loop(const Gemv &g, int lo, int hi, unsigned otag) {
+    const uint4 *act4 = reinterpret_cast<const uint4 *>(U);
     const int R = tile_rows(g);
     const int K = g.K, n8 = K / 8;
     const size_t rowb = (size_t)K * 2;
@@ -604,104 +759,102 @@ template <int NB> struct Consumer {
     for (int r0 = lo; r0 < hi; r0 += R, parity ^= 1) {
       const int n = min(R, hi - r0);
       const int pairs = (n + 1) >> 1;
-      int S = 1;
-      while (S < kWarps && pairs * S * 2 <= kWarps) S <<= 1;
       const char *slotp = wait_full();
-      const int seg = warp % S;
-      // S > 1 only when all pairs fit in one pass (pairs * S <= kWarps)
-      for (int pbase = 0; pbase < pairs; pbase += kWarps / S) {
-        const int pair = pbase + warp / S;
-        const bool active = slotp != nullptr && pair < pairs;
-        float a0[NB], a1[NB], c0[NB], c1[NB];
-#pragma unroll
-        for (int b = 0; b < NB; ++b) { a0[b] = a1[b] = c0[b] = c1[b] = 0.f; }
-        if (active) {
+      if (pairs >= kWarps) {
+        // fast path
+        for (int pair = warp; slotp && pair < pairs; pair += kWarps) {
           const int rA = 2 * pair, rB = min(rA + 1, n - 1);
           const uint4 *wA = reinterpret_cast<const uint4 *>(slotp + rA * rowb);
           const uint4 *wB = reinterpret_cast<const uint4 *>(slotp + rB * rowb);
           const uint4 *uA = reinterpret_cast<const uint4 *>(slotp + (n + rA) * rowb);
           const uint4 *uB = reinterpret_cast<const uint4 *>(slotp + (n + rB) * rowb);
-          const int cb = (n8 * seg) / S, ce = (n8 * (seg + 1)) / S;
-          const uint4 *act4 = reinterpret_cast<const uint4 *>(act);
-          if (g.paired) {
+          const float2 r = gemv_pair<PAIRED, NB>(wA, wB, uA, uB, act4, n8, 0, n8);
+          const int row = rA + (second ? 1 : 0);
+          if (bsel < NB && bsel < p.B && row < n) epilogue(EPI, bsel, r0 + row, r.x, r.y, lo, otag);
+        }
+        release();
+        continue;
+      }
+      int S = 1;
+      while (S < kWarps && pairs * S * 2 <= kWarps) S <<= 1;
+      const int seg = warp % S;
+      const int pair = warp / S;
+      const bool active = slotp != nullptr && pair < pairs;
+      float a0[NB], a1[NB], c0[NB], c1[NB];
+#pragma unroll
+      for (int b = 0; b < NB; ++b) { a0[b] = a1[b] = c0[b] = c1[b] = 0.f; }
+      if (active) {
+        const int rA = 2 * pair, rB = min(rA + 1, n - 1);
+        const uint4 *wA = reinterpret_cast<const uint4 *>(slotp + rA * rowb);
+        const uint4 *wB = reinterpret_cast<const uint4 *>(slotp + rB * rowb);
+        const uint4 *uA = reinterpret_cast<const uint4 *>(slotp + (n + rA) * rowb);
+        const uint4 *uB = reinterpret_cast<const uint4 *>(slotp + (n + rB) * rowb);
+        const int cb = (n8 * seg) / S, ce = (n8 * (seg + 1)) / S;
 #pragma unroll 2
-            for (int j = cb + lane; j < ce; j += 32) {
-              const uint4 wa = wA[j], wb = wB[j], ua = uA[j], ub = uB[j];
-#pragma unroll
-              for (int b = 0; b < NB; ++b) {
-                const uint4 x = act4[b * n8 + j];
-                a0[b] = dot8_bf16(wa, x, a0[b]);
-                c0[b] = dot8_bf16(wb, x, c0[b]);
-                a1[b] = dot8_bf16(ua, x, a1[b]);
-                c1[b] = dot8_bf16(ub, x, c1[b]);
-              }
-            }
-          } else {
-#pragma unroll 4
-            for (int j = cb + lane; j < ce; j += 32) {
-              const uint4 wa = wA[j], wb = wB[j];
-#pragma unroll
-              for (int b = 0; b < NB; ++b) {
-                const uint4 x = act4[b * n8 + j];
-                a0[b] = dot8_bf16(wa, x, a0[b]);
-                c0[b] = dot8_bf16(wb, x, c0[b]);
-              }
-            }
-          }
+        for (int j = cb + lane; j < ce; j += 32) {
+          const uint4 wa = wA[j], wb = wB[j];
+          uint4 ua = make_uint4(0, 0, 0, 0), ub = ua;
+          if (PAIRED) { ua = uA[j]; ub = uB[j]; }
 #pragma unroll
           for (int b = 0; b < NB; ++b) {
-            a0[b] = warp_sum(a0[b]);
-            c0[b] = warp_sum(c0[b]);
-            if (g.paired) { a1[b] = warp_sum(a1[b]); c1[b] = warp_sum(c1[b]); }
-          }
-        }
-        float v = 0.f, v2 = 0.f;
-#pragma unroll
-        for (int b = 0; b < NB; ++b)
-          if (bsel == b) { v = second ? c0[b] : a0[b]; v2 = second ? c1[b] : a1[b]; }
-        if (S > 1) {
-          float *part = red + RED_PART + parity * 256;  // [warp][2 rows][NB][2]
-          if (active && bsel < NB) {
-            float *q = part + ((warp * 2 + (second ? 1 : 0)) * NB + bsel) * 2;
-            q[0] = v;
-            q[1] = v2;
-          }
-          csync();
-          if (active && seg == 0 && bsel < NB) {
-            v = v2 = 0.f;
-            for (int sgi = 0; sgi < S; ++sgi) {
-              const float *q = part + (((pair * S + sgi) * 2 + (second ? 1 : 0)) * NB + bsel) * 2;
-              v += q[0];
-              v2 += q[1];
+            const uint4 x = act4[b * n8 + j];
+            a0[b] = dot8_bf16(wa, x, a0[b]);
+            c0[b] = dot8_bf16(wb, x, c0[b]);
+            if (PAIRED) {
+              a1[b] = dot8_bf16(ua, x, a1[b]);
+              c1[b] = dot8_bf16(ub, x, c1[b]);
             }
           }
         }
-        if (active && seg == 0 && bsel < NB && bsel < p.B) {
-          const int row = 2 * pair + (second ? 1 : 0);
-          if (row < n) epilogue(epi, bsel, r0 + row, v, v2, lo, hi - lo);
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          a0[b] = warp_sum(a0[b]);
+          c0[b] = warp_sum(c0[b]);
+          if (PAIRED) { a1[b] = warp_sum(a1[b]); c1[b] = warp_sum(c1[b]); }
         }
+      }
+      float v = 0.f, v2 = 0.f;
+#pragma unroll
+      for (int b = 0; b < NB; ++b)
+        if (bsel == b) { v = second ? c0[b] : a0[b]; v2 = second ? c1[b] : a1[b]; }
+      float *part = red + RED_PART + parity * 256;  // [warp][2 rows][NB][2]
+      if (active && bsel < NB) {
+        float *q = part + ((warp * 2 + (second ? 1 : 0)) * NB + bsel) * 2;
+        q[0] = v;
+        q[1] = v2;
+      }
+      csync();
+      if (active && seg == 0 && bsel < NB) {
+        v = v2 = 0.f;
+        for (int sgi = 0; sgi < S; ++sgi) {
+          const float *q = part + (((pair * S + sgi) * 2 + (second ? 1 : 0)) * NB + bsel) * 2;
+          v += q[0];
+          v2 += q[1];
+        }
+        const int row = 2 * pair + (second ? 1 : 0);
+        if (bsel < p.B && row < n) epilogue(EPI, bsel, r0 + row, v, v2, lo, otag);
       }
       release();
     }
-    if (epi == EPI_RESID) h_ready = true;
-    if (epi == EPI_LOGITS) argmax_finish();
   }
 
   __device__ __forceinline__ void epilogue(int epi, int b, int row, float v, float v2, int lo,
-                                           int nres) {
+                                           unsigned tg) {
     switch (epi) {
     case EPI_STORE:
-      p.proj[(size_t)b * p.pstride + row] = tobf(v);
+      p.proj[(size_t)b * p.pstride + row] = tagged(v, tg);
       break;
     case EPI_RESID: {
-      const float hv = red[RED_RESID + b * nres + (row - lo)];
-      p.h[(size_t)b * p.H + row] = tobf(hv + rbf(v));
+      float *hr = hres + b * kResRows + (row - lo);
+      const float hv = rbf(*hr + rbf(v));
+      *hr = hv;
+      p.h[(size_t)b * p.H + row] = tagged(hv, tg);
       break;
     }
     case EPI_GATEUP: {
       const float gt = rbf(v), up = rbf(v2);
       const float s = rbf(gt / (1.f + expf(-gt)));
-      p.act[(size_t)b * p.I + row] = tobf(s * up);
+      p.act[(size_t)b * p.I + row] = tagged(s * up, tg);
       break;
     }
     case EPI_LOGITS: {
@@ -713,14 +866,14 @@ template <int NB> struct Consumer {
     }
   }
 
-  // Per-CTA argmax -> workspace; the last CTA to finish reduces all CTAs, writes the tokens and
-  // resets the barrier counters and its own ticket for the next launch.
+  // Per-CTA argmax -> workspace; the last CTA to finish reduces all CTAs, writes the tokens,
+  // advances the launch epoch and resets its own ticket for the next launch.
   __device__ void argmax_finish() {
     float *sv = red;                                  // [kWarps][2][NB]
     int *si = reinterpret_cast<int *>(red + 2 * kWarps * NB);
     const int bsel = lane & 15;
     if (bsel < NB) {
-      const int k = (warp * 2 + (second_half() ? 1 : 0)) * NB + bsel;
+      const int k = (warp * 2 + (lane >= 16 ? 1 : 0)) * NB + bsel;
       sv[k] = am_v;
       si[k] = am_i;
     }
@@ -745,29 +898,38 @@ template <int NB> struct Consumer {
     csync();
     if (hdr->is_last) {
       __threadfence();
-      if (tid < p.B && p.tokens) {
+      // warp b reduces batch row b over all CTAs: lanes load candidates in parallel
+      if (warp < p.B && warp < NB && p.tokens) {
         float bv = -INFINITY;
         int bi = 0x7fffffff;
-        for (int c = 0; c < p.ncta; ++c) {
-          const float v = ldcg_f(p.am_v + c * XB_MAX_BATCH + tid);
-          const int i = __ldcg(p.am_i + c * XB_MAX_BATCH + tid);
+        for (int c = lane; c < p.ncta; c += 32) {
+          const float v = ldcg_f(p.am_v + c * XB_MAX_BATCH + warp);
+          const int i = __ldcg(p.am_i + c * XB_MAX_BATCH + warp);
           if (argmax_better(v, i, bv, bi)) { bv = v; bi = i; }
         }
-        p.tokens[tid] = bi;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (argmax_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) p.tokens[warp] = bi;
       }
-      // every CTA has passed its last grid barrier before taking a ticket
-      if (tid < 8) p.ctrl[CTL_BAR + tid * 32] = 0u;
-      if (tid == 0) atomicExch(p.ctrl + CTL_DONE, 0u);
+      if (tid == 0) {
+        // every CTA has consumed all tagged inputs of this launch before taking a ticket
+        p.ctrl[CTL_EPOCH] = epoch + 1u;  // also after an abort: stale tags never match again
+        atomicExch(p.ctrl + CTL_DONE, 0u);
+      }
     }
   }
-  __device__ __forceinline__ bool second_half() const { return lane >= 16; }
 
   // ---- Gated DeltaNet recurrent step (compiler/qwen35/kernels/recurrent.py:20-124) ---------
-  // Work item = (row b, value head h, 16-column tile t of the 128x128 state). Every global load
-  // of an item (state slice, conv windows and taps, projections, gate scalars) is issued up front.
-  __device__ void delta(int l) {
+  // Work item = (row b, value head h, 16-column tile t of the 128x128 state). The state slice,
+  // conv windows and taps are loaded up front; the projections of this head are polled.
+  __device__ __forceinline__ void delta(int l) {
     stage_begin();
     const XbLayerWeights &w = p.layers[l];
+    const unsigned tg = tag(l, 0);
     const int HK = p.HK, HV = p.HV, DK = p.DK;
     const int CH = (2 * HK + HV) * DK, CW = p.CW;
     const int group = HV / HK;
@@ -796,36 +958,36 @@ template <int NB> struct Consumer {
       float S[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) S[i] = S_in[(size_t)(rbase + i) * DK + col];
+      unsigned *core = p.core + (size_t)b * HV * DK + h * DK + t * 16;
+      uint2 *ssq = p.ssq + ((size_t)b * HV + h) * 8 + t;
       if (p.q_len[b] == 0) {
         // Empty row: replacement state equals the input state (a no-op when in place).
 #pragma unroll
         for (int i = 0; i < 8; ++i) S_out[(size_t)(rbase + i) * DK + col] = S[i];
-        if (tid < 16) p.core[(size_t)b * HV * DK + h * DK + t * 16 + tid] = tobf(0.f);
-        if (tid == 0) p.ssq[((size_t)b * HV + h) * 8 + t] = 0.f;
+        if (tid < 16) core[tid] = tagged(0.f, tg);
+        if (tid == 0) *ssq = make_uint2(0u, tg);
         continue;
       }
       const bf16 *cin = conv_in_all + (size_t)b * CH * CW;
-      const bf16 *x = p.proj + (size_t)b * p.pstride;
+      const unsigned *x = p.proj + (size_t)b * p.pstride;
       // conv channels: q (tid < 128) or k (tid >= 128) of key head kh; v channel for tid < 16
       const int chq = tid < DK ? kh * DK + tid : (HK + kh) * DK + (tid - DK);
       const int chv = (2 * HK + h) * DK + t * 16 + (tid & 15);
       const uint2 cq = *reinterpret_cast<const uint2 *>(cin + (size_t)chq * CW);
       const uint2 wq = *reinterpret_cast<const uint2 *>(cw + (size_t)chq * CW);
-      const float xq = bf(ldcg_bf(x + chq));
       uint2 cv = make_uint2(0, 0), wvv = make_uint2(0, 0);
-      float xv = 0.f;
       if (tid < 16) {
         cv = *reinterpret_cast<const uint2 *>(cin + (size_t)chv * CW);
         wvv = *reinterpret_cast<const uint2 *>(cw + (size_t)chv * CW);
-        xv = bf(ldcg_bf(x + chv));
       }
       float gsc = 0.f;
       if (warp == 0) {
-        if (lane == 0) gsc = bf(ldcg_bf(x + CH + HV * DK + h));           // b
-        else if (lane == 1) gsc = bf(ldcg_bf(x + CH + HV * DK + HV + h));  // a
-        else if (lane == 2) gsc = bf(((const bf16 *)w.dt_bias)[h]);
+        if (lane == 2) gsc = bf(((const bf16 *)w.dt_bias)[h]);
         else if (lane == 3) gsc = bf(((const bf16 *)w.a_log)[h]);
       }
+      const float xq = bf_lo(poll1(x + chq, tg));
+      const float xv = tid < 16 ? bf_lo(poll1(x + chv, tg)) : 0.f;
+      if (warp == 0 && lane < 2) gsc = bf_lo(poll1(x + CH + HV * DK + lane * HV + h, tg));  // b, a
       // causal conv (width 4) over [conv[1..3], x] + SiLU, rounded as recurrent.py:32-58
       auto conv = [](uint2 cs, uint2 ws, float xx) -> float {
         float tot = 0.f;
@@ -890,20 +1052,25 @@ template <int NB> struct Consumer {
 #pragma unroll
         for (int i = 0; i < kWarps; ++i) out += po[i * 16 + tid];
         const float ob = rbf(out);
-        p.core[(size_t)b * HV * DK + h * DK + t * 16 + tid] = tobf(ob);
+        core[tid] = tagged(ob, tg);
         float sq = ob * ob;
 #pragma unroll
         for (int o2 = 8; o2; o2 >>= 1) sq += __shfl_xor_sync(0x0000ffffu, sq, o2);
-        if (tid == 0) p.ssq[((size_t)b * HV + h) * 8 + t] = sq;
+        if (tid == 0) *ssq = make_uint2(__float_as_uint(sq), tg);
       }
     }
   }
 
   // ---- attention: q/k norm, RoPE, KV append, split-KV partials ----------------------------
-  __device__ void attn(int l) {
+  // Work item = (row b, KV head, split of the populated prefix). Warp w serves query head
+  // w % G over positions j with (j - j0) / 1 % P == w / G (P = kWarps / G position lanes); the
+  // P partial softmax states of each head are merged in shared memory.
+  __device__ __forceinline__ void attn(int l) {
     stage_begin();
     const XbLayerWeights &w = p.layers[l];
+    const unsigned tg = tag(l, 0);
     const int D = p.D, HQ = p.HQ, HKV = p.HKV, G = HQ / HKV, RD = p.RD;
+    const int P = kWarps / G;
     const bool q35 = p.family == XB_FAMILY_QWEN35;
     const int qrow = q35 ? 2 * D : D;
     const int koff = HQ * qrow, voff = koff + HKV * D;
@@ -913,7 +1080,7 @@ template <int NB> struct Consumer {
     float *qs = reinterpret_cast<float *>(U);        // [G][D]
     float *kn = qs + G * D;                          // [D]
     float *vn = kn + D;                              // [D]
-    float *mg = vn + D;                              // [kWarps][G][D+2]
+    float *mg = vn + D;                              // [kWarps][D+2]
     bf16 *kc_all = (bf16 *)p.sa[l];
     bf16 *vc_all = (bf16 *)p.sb[l];
     const float scale = p.att_scale;
@@ -925,18 +1092,24 @@ template <int NB> struct Consumer {
       const int kvl = p.kv_len[b];
       const long long pos = position(p, b);
       const int chunk = (kvl + splits - 1) / splits;
-      const int j0 = s * chunk, j1 = min(kvl, j0 + chunk);
-      const bf16 *x = p.proj + (size_t)b * p.pstride;
+      const int j0 = min(kvl, s * chunk), j1 = min(kvl, j0 + chunk);
+      const unsigned *x = p.proj + (size_t)b * p.pstride;
       // warps 0..G-1: query heads; warp G: new key; warp G+1: new value
       if (warp <= G) {
         const bool isk = warp == G;
         const int hq = kvh * G + warp;
-        const bf16 *src = isk ? x + koff + kvh * D : x + hq * qrow;
+        const unsigned *src = isk ? x + koff + kvh * D : x + hq * qrow;
         const bf16 *nw = (const bf16 *)(isk ? w.k_norm : w.q_norm);
         float v[8], ss = 0.f;
 #pragma unroll
+        for (int e4 = 0; e4 < 8; e4 += 4)
+          if (e4 < EPL) {
+            const uint4 q4 = poll4(src + lane * EPL + e4, tg);
+            v[e4] = bf_lo(q4.x); v[e4 + 1] = bf_lo(q4.y); v[e4 + 2] = bf_lo(q4.z); v[e4 + 3] = bf_lo(q4.w);
+          }
+#pragma unroll
         for (int e = 0; e < 8; ++e)
-          if (e < EPL) { v[e] = bf(ldcg_bf(src + lane * EPL + e)); ss = fmaf(v[e], v[e], ss); }
+          if (e < EPL) ss = fmaf(v[e], v[e], ss);
         ss = warp_sum(ss);
         const float r = rsqrtf(ss / (float)D + p.eps);
         float *dst = isk ? kn : qs + warp * D;
@@ -968,8 +1141,14 @@ template <int NB> struct Consumer {
           if (e < EPL) dst[lane * EPL + e] = v[e];
       } else if (warp == G + 1) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          if (e < EPL) vn[lane * EPL + e] = bf(ldcg_bf(x + voff + kvh * D + lane * EPL + e));
+        for (int e4 = 0; e4 < 8; e4 += 4)
+          if (e4 < EPL) {
+            const uint4 q4 = poll4(x + voff + kvh * D + lane * EPL + e4, tg);
+            vn[lane * EPL + e4] = bf_lo(q4.x);
+            vn[lane * EPL + e4 + 1] = bf_lo(q4.y);
+            vn[lane * EPL + e4 + 2] = bf_lo(q4.z);
+            vn[lane * EPL + e4 + 3] = bf_lo(q4.w);
+          }
       }
       csync();
       bf16 *kc = kc_all + (((size_t)b * HKV + kvh) * p.C) * D;
@@ -979,89 +1158,95 @@ template <int NB> struct Consumer {
         kc[(size_t)pos * D + tid] = tobf(kn[tid]);
         vc[(size_t)pos * D + tid] = tobf(vn[tid]);
       }
-      // split-KV partial over positions [j0, j1): warp-per-position online softmax
-      float q[4][8], o[4][8], m[4], lsum[4];
+      // split-KV partial over positions [j0, j1) for query head g = warp % G
+      const int g = warp % G, lane_pos = warp / G;
+      float q[8], o[8];
+      float m = -INFINITY, lsum = 0.f;
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        m[g] = -INFINITY; lsum[g] = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          o[g][e] = 0.f;
-          q[g][e] = (g < G && e < EPL) ? qs[g * D + lane * EPL + e] : 0.f;
-        }
+      for (int e = 0; e < 8; ++e) {
+        o[e] = 0.f;
+        q[e] = e < EPL ? qs[g * D + lane * EPL + e] : 0.f;
       }
-      for (int j = j0 + warp; j < j1; j += kWarps) {
+      // one position per step, the next position's K/V rows prefetched (kept packed)
+      uint4 kraw = make_uint4(0, 0, 0, 0), vraw = kraw;
+      auto fetch = [&](int j, uint4 &kr4, uint4 &vr4) {
+        if (j < j1 && j != pos) {
+          if (EPL == 8) {
+            kr4 = ldg_u4(kc + (size_t)j * D + lane * 8);
+            vr4 = ldg_u4(vc + (size_t)j * D + lane * 8);
+          } else {
+            const uint2 k2 = ldg_u2(kc + (size_t)j * D + lane * 4);
+            const uint2 v2 = ldg_u2(vc + (size_t)j * D + lane * 4);
+            kr4 = make_uint4(k2.x, k2.y, 0, 0);
+            vr4 = make_uint4(v2.x, v2.y, 0, 0);
+          }
+        }
+      };
+      fetch(j0 + lane_pos, kraw, vraw);
+      for (int j = j0 + lane_pos; j < j1; j += P) {
+        const uint4 kcur = kraw, vcur = vraw;
+        fetch(j + P, kraw, vraw);
         float kf[8], vf[8];
         if (j == pos) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            if (e < EPL) { kf[e] = kn[lane * EPL + e]; vf[e] = vn[lane * EPL + e]; }
-        } else if (EPL == 8) {
-          unpack8(ldnc_u4(kc + (size_t)j * D + lane * 8), kf);
-          unpack8(ldnc_u4(vc + (size_t)j * D + lane * 8), vf);
+          for (int e = 0; e < 8; ++e) {
+            kf[e] = e < EPL ? kn[lane * EPL + e] : 0.f;
+            vf[e] = e < EPL ? vn[lane * EPL + e] : 0.f;
+          }
         } else {
-          const uint2 ku = ldnc_u2(kc + (size_t)j * D + lane * 4);
-          const uint2 vu = ldnc_u2(vc + (size_t)j * D + lane * 4);
-          kf[0] = bf_lo(ku.x); kf[1] = bf_hi(ku.x); kf[2] = bf_lo(ku.y); kf[3] = bf_hi(ku.y);
-          vf[0] = bf_lo(vu.x); vf[1] = bf_hi(vu.x); vf[2] = bf_lo(vu.y); vf[3] = bf_hi(vu.y);
+          unpack8(kcur, kf);
+          unpack8(vcur, vf);
         }
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          if (g >= G) break;
-          float sc = 0.f;
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            if (e < EPL) sc = fmaf(q[g][e], kf[e], sc);
-          sc = warp_sum(sc) * scale;
-          const float mn = fmaxf(m[g], sc);
-          const float corr = expf(m[g] - mn);
-          const float pe = expf(sc - mn);
-          lsum[g] = lsum[g] * corr + pe;
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            if (e < EPL) o[g][e] = fmaf(pe, vf[e], o[g][e] * corr);
-          m[g] = mn;
-        }
-      }
-      // merge the kWarps partial states
-      const int MS = D + 2;
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        if (g >= G) break;
-        float *mw = mg + ((size_t)warp * G + g) * MS;
+        float sc = 0.f;
 #pragma unroll
         for (int e = 0; e < 8; ++e)
-          if (e < EPL) mw[lane * EPL + e] = o[g][e];
-        if (lane == 0) { mw[D] = m[g]; mw[D + 1] = lsum[g]; }
+          if (e < EPL) sc = fmaf(q[e], kf[e], sc);
+        sc = warp_sum(sc) * scale;
+        const float mn = fmaxf(m, sc);
+        const float corr = expf(m - mn);
+        const float pe = expf(sc - mn);
+        lsum = lsum * corr + pe;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < EPL) o[e] = fmaf(pe, vf[e], o[e] * corr);
+        m = mn;
       }
+      // merge the P partial states of each head
+      const int MS = D + 2;
+      float *mw = mg + (size_t)warp * MS;
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e < EPL) mw[lane * EPL + e] = o[e];
+      if (lane == 0) { mw[D] = m; mw[D + 1] = lsum; }
       csync();
       for (int idx = tid; idx < G * D; idx += kCT) {
-        const int g = idx / D, d = idx % D;
+        const int gg = idx / D, d = idx % D;
         float M = -INFINITY;
-        for (int i = 0; i < kWarps; ++i) M = fmaxf(M, mg[((size_t)i * G + g) * MS + D]);
+        for (int i = 0; i < P; ++i) M = fmaxf(M, mg[(size_t)(i * G + gg) * MS + D]);
         float O = 0.f, Lw = 0.f;
         if (M != -INFINITY) {
-          for (int i = 0; i < kWarps; ++i) {
-            const float *mw = mg + ((size_t)i * G + g) * MS;
-            const float mi = mw[D];
+          for (int i = 0; i < P; ++i) {
+            const float *ms = mg + (size_t)(i * G + gg) * MS;
+            const float mi = ms[D];
             if (mi == -INFINITY) continue;
             const float f = expf(mi - M);
-            O = fmaf(mw[d], f, O);
-            Lw = fmaf(mw[D + 1], f, Lw);
+            O = fmaf(ms[d], f, O);
+            Lw = fmaf(ms[D + 1], f, Lw);
           }
         }
-        const int hq = kvh * G + g;
+        const int hq = kvh * G + gg;
         const size_t base = ((size_t)b * HQ + hq) * splits + s;
-        p.att_o[base * D + d] = O;
-        if (d == 0) { p.att_ml[base * 2] = M; p.att_ml[base * 2 + 1] = Lw; }
+        p.att_o[base * D + d] = make_uint2(__float_as_uint(O), tg);
+        if (d == 0) p.att_ml[base] = make_uint4(__float_as_uint(M), tg, __float_as_uint(Lw), tg);
       }
       csync();
     }
   }
 
   // ---- combine split partials, then the Qwen3.5 sigmoid output gate -----------------------
-  __device__ void comb(int) {
+  __device__ __forceinline__ void comb(int l) {
     stage_begin();
+    const unsigned tg = tag(l, 0);
     const int D = p.D, HQ = p.HQ, splits = p.splits;
     const bool q35 = p.family == XB_FAMILY_QWEN35;
     const int chunks = D / 32;
@@ -1075,27 +1260,52 @@ template <int NB> struct Consumer {
       const int hq = (item / chunks) % HQ;
       const int ck = item % chunks;
       const int d = ck * 32 + lane;
-      bf16 *dst = p.att_out + (size_t)b * HQ * D + hq * D;
+      unsigned *dst = p.att_out + (size_t)b * HQ * D + hq * D;
       if (p.q_len[b] == 0) {
-        if (warp == 0) dst[d] = tobf(0.f);
+        if (warp == 0) dst[d] = tagged(0.f, tg);
         continue;
       }
       const size_t base = ((size_t)b * HQ + hq) * splits;
       for (int s = tid; s < splits; s += kCT) {
-        ms[s] = ldcg_f(p.att_ml + (base + s) * 2);
-        ls[s] = ldcg_f(p.att_ml + (base + s) * 2 + 1);
+        uint4 v = ldcg_u4(p.att_ml + base + s);
+        if (v.y != tg || v.w != tg) {
+          uint64_t t0 = 0;
+          for (unsigned spins = 1;; ++spins) {
+            v = ld_poll_u4(p.att_ml + base + s);
+            if (v.y == tg && v.w == tg) break;
+            if ((spins & 15u) == 0 && give_up(t0)) break;
+          }
+        }
+        ms[s] = __uint_as_float(v.x);
+        ls[s] = __uint_as_float(v.z);
       }
       csync();
       float M = -INFINITY;
       for (int s = 0; s < splits; ++s) M = fmaxf(M, ms[s]);
       float O = 0.f, Lw = 0.f;
-      if (M != -INFINITY)
-        for (int s = warp; s < splits; s += kWarps) {
-          if (ms[s] == -INFINITY) continue;
-          const float f = expf(ms[s] - M);
-          O = fmaf(ldcg_f(p.att_o + (base + s) * D + d), f, O);
-          Lw = fmaf(ls[s], f, Lw);
+      if (M != -INFINITY) {
+        constexpr int MSP = 10;  // splits handled per pass per warp
+        for (int s0 = warp; s0 < splits; s0 += kWarps * MSP) {
+          uint2 vo[MSP];
+#pragma unroll
+          for (int i = 0; i < MSP; ++i) {
+            const int s = s0 + i * kWarps;
+            vo[i] = (s < splits && ms[s] != -INFINITY) ? __ldcg(p.att_o + (base + s) * D + d)
+                                                       : make_uint2(0u, tg);
+          }
+#pragma unroll
+          for (int i = 0; i < MSP; ++i) {
+            const int s = s0 + i * kWarps;
+            if (s >= splits || ms[s] == -INFINITY) continue;
+            const float ov = vo[i].y == tg ? __uint_as_float(vo[i].x)
+                                           : repoll1f(p.att_o + (base + s) * D + d, tg, abort_flag(),
+                                                      p.ctrl);
+            const float f = expf(ms[s] - M);
+            O = fmaf(ov, f, O);
+            Lw = fmaf(ls[s], f, Lw);
+          }
         }
+      }
       po[warp * 32 + lane] = O;
       if (lane == 0) pl[warp] = Lw;
       csync();
@@ -1104,18 +1314,19 @@ template <int NB> struct Consumer {
         for (int i = 0; i < kWarps; ++i) { Ot += po[i * 32 + lane]; Lt += pl[i]; }
         float y = Lt > 0.f ? rbf(Ot / Lt) : 0.f;
         if (q35) {
-          const float gt = bf(ldcg_bf(p.proj + (size_t)b * p.pstride + hq * 2 * D + D + d));
-          const float sg = rbf(1.f / (1.f + expf(-gt)));
+          const float gtv =
+              bf_lo(poll1(p.proj + (size_t)b * p.pstride + hq * 2 * D + D + d, tg));
+          const float sg = rbf(1.f / (1.f + expf(-gtv)));
           y = rbf(y * sg);
         }
-        dst[d] = tobf(y);
+        dst[d] = tagged(y, tg);
       }
       csync();
     }
   }
 };
 
-template <class V> __device__ void walk_step(const StepParams &p, V &v) {
+template <class V> __device__ __forceinline__ void walk_step(const StepParams &p, V &v) {
   for (int l = 0; l < p.L; ++l) {
     if (is_delta(p, l)) {
       v.gemv(l, ST_IN_DELTA);
@@ -1137,7 +1348,8 @@ template <int NB>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ StepParams p) {
   extern __shared__ __align__(1024) char smem[];
   SmemHdr *hdr = reinterpret_cast<SmemHdr *>(smem);
-  float *red = reinterpret_cast<float *>(smem + kHdrBytes);
+  float *hres = reinterpret_cast<float *>(smem + kHdrBytes);
+  float *red = reinterpret_cast<float *>(smem + kHdrBytes + kResBytes);
   char *U = smem + kUOffset;
   char *ring = U + p.ubytes;
   if (threadIdx.x == 0) {
@@ -1147,6 +1359,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     }
     hdr->abort = 0;
     hdr->is_last = 0;
+    hdr->epoch = ld_volatile(p.ctrl + CTL_EPOCH);
     mbar_fence_init();
   }
   // validate token ids once (out-of-range ids are recorded and read as id 0 nowhere: abort)
@@ -1182,7 +1395,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       }
     }
   } else if (!bad) {
-    Consumer<NB> c(p, hdr, red, U, ring);
+    Consumer<NB> c(p, hdr, red, hres, U, ring);
     walk_step(p, c);
     c.trace_end();
   }
@@ -1236,16 +1449,16 @@ static WsLayout ws_layout(const XbGeometry &g, int max_batch, int ncta) {
   L.max_splits = ncta;
   size_t off = 0;
   auto take = [&](size_t bytes) { size_t o = off; off += (bytes + 255) & ~size_t(255); return o; };
-  L.ctrl = take(CTL_WORDS * 4);
-  L.h = take((size_t)B * g.hidden * 2);
-  L.proj = take((size_t)B * L.pstride * 2);
+  L.ctrl = take(CTL_TOTAL * 4);
+  L.h = take((size_t)B * g.hidden * 4);
+  L.proj = take((size_t)B * L.pstride * 4);
   const int vdim = q35 ? g.lin_value_heads * g.lin_head_dim : 8;
-  L.core = take((size_t)B * vdim * 2);
-  L.ssq = take((size_t)B * (q35 ? g.lin_value_heads : 1) * 8 * 4);
-  L.att_o = take((size_t)B * g.num_q_heads * L.max_splits * g.head_dim * 4);
-  L.att_ml = take((size_t)B * g.num_q_heads * L.max_splits * 2 * 4);
-  L.att_out = take((size_t)B * g.num_q_heads * g.head_dim * 2);
-  L.act = take((size_t)B * g.intermediate * 2);
+  L.core = take((size_t)B * vdim * 4);
+  L.ssq = take((size_t)B * (q35 ? g.lin_value_heads : 1) * 8 * 8);
+  L.att_o = take((size_t)B * g.num_q_heads * L.max_splits * g.head_dim * 8);
+  L.att_ml = take((size_t)B * g.num_q_heads * L.max_splits * 16);
+  L.att_out = take((size_t)B * g.num_q_heads * g.head_dim * 4);
+  L.act = take((size_t)B * g.intermediate * 4);
   L.am_v = take((size_t)ncta * XB_MAX_BATCH * 4);
   L.am_i = take((size_t)ncta * XB_MAX_BATCH * 4);
   L.total = off;
@@ -1284,6 +1497,8 @@ static int check_geometry(const XbGeometry &g) {
     if (g.lin_value_heads * g.lin_head_dim > 8192 || 2 * g.lin_head_dim > kCT)
       return fail(XB_ERR_UNSUPPORTED, "DeltaNet value width too large");
   }
+  if (g.hidden > kResRows * 148)
+    return fail(XB_ERR_UNSUPPORTED, "hidden size too large for the per-CTA residual rows");
   // every GEMV must fit at least one row (two for gate/up) into a 32 KB ring slot
   const int kmax = std::max(g.intermediate, std::max(g.hidden, g.num_q_heads * g.head_dim));
   if (kmax * 2 > kSlot || g.hidden * 4 > kSlot)
@@ -1298,7 +1513,7 @@ static size_t ubytes_for(const XbGeometry &g, int NB) {
   if (q35) kmax = std::max(kmax, g.lin_value_heads * g.lin_head_dim);
   const size_t act = (size_t)NB * kmax * 2;
   const int G = g.num_q_heads / g.num_kv_heads;
-  const size_t att = ((size_t)G * g.head_dim + 2 * g.head_dim + (size_t)kWarps * G * (g.head_dim + 2)) * 4;
+  const size_t att = ((size_t)G * g.head_dim + 2 * g.head_dim + (size_t)kWarps * (g.head_dim + 2)) * 4;
   const size_t u = std::max(act, att);
   return (u + 127) & ~size_t(127);
 }
@@ -1435,7 +1650,7 @@ int xb_workspace_check(void *workspace, void *stream, int32_t *device_error) {
   XB_CUDA(cudaMemcpy(&err, (unsigned *)workspace + CTL_ERR, 4, cudaMemcpyDeviceToHost));
   if (device_error) *device_error = (int32_t)err;
   if (err) {
-    // reset the control words so the workspace can be reused
+    // reset the control words so the workspace can be reused (the epoch word is kept)
     XB_CUDA(cudaMemset(workspace, 0, CTL_WORDS * 4));
     return fail(XB_ERR_DEVICE, "device-side error code " + std::to_string(err));
   }
@@ -1488,10 +1703,10 @@ int xb_decode_step(const XbModel *model, const XbStepArgs *args, void *workspace
   p.dk_scale = (float)(1.0 / std::sqrt((double)p.DK));
   p.att_scale = (float)(1.0 / std::sqrt((double)g.head_dim));
   p.pstride = Lb.pstride;
-  // split-KV: enough (row, kv head, split) items to cover every SM, >= 16 positions per split
+  // split-KV: enough (row, kv head, split) items to cover every SM, >= 4 positions per split
   int splits = std::max(1, ncta / std::max(1, active * g.num_kv_heads));
-  splits = std::min(splits, std::max(1, (max_kv + 15) / 16));
-  splits = std::min(splits, std::min(Lb.max_splits, 256));
+  splits = std::min(splits, std::max(1, (max_kv + 3) / 4));
+  splits = std::min(splits, std::min(Lb.max_splits, 160));
   p.splits = splits;
   p.ncta = ncta;
   p.B = B;
@@ -1528,14 +1743,14 @@ int xb_decode_step(const XbModel *model, const XbStepArgs *args, void *workspace
   p.tokens = args->next_tokens;
   char *ws = (char *)workspace;
   p.ctrl = (unsigned *)(ws + Lb.ctrl);
-  p.h = (bf16 *)(ws + Lb.h);
-  p.proj = (bf16 *)(ws + Lb.proj);
-  p.core = (bf16 *)(ws + Lb.core);
-  p.ssq = (float *)(ws + Lb.ssq);
-  p.att_o = (float *)(ws + Lb.att_o);
-  p.att_ml = (float *)(ws + Lb.att_ml);
-  p.att_out = (bf16 *)(ws + Lb.att_out);
-  p.act = (bf16 *)(ws + Lb.act);
+  p.h = (unsigned *)(ws + Lb.h);
+  p.proj = (unsigned *)(ws + Lb.proj);
+  p.core = (unsigned *)(ws + Lb.core);
+  p.ssq = (uint2 *)(ws + Lb.ssq);
+  p.att_o = (uint2 *)(ws + Lb.att_o);
+  p.att_ml = (uint4 *)(ws + Lb.att_ml);
+  p.att_out = (unsigned *)(ws + Lb.att_out);
+  p.act = (unsigned *)(ws + Lb.act);
   p.am_v = (float *)(ws + Lb.am_v);
   p.am_i = (int *)(ws + Lb.am_i);
   p.trace = g_trace;

@@ -13,6 +13,8 @@ typedef __nv_bfloat16 bf16;
 // Bounded waits: every spin in these kernels gives up after this many nanoseconds, records an
 // error word in the workspace and lets the kernel return (no trap, no endless loop).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// Waits shorter than this never leave the fast path (no global loads besides the polled data).
+constexpr uint64_t kSlowWaitNs = 20000ull;
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
@@ -82,6 +84,48 @@ __device__ __forceinline__ uint2 ldnc_u2(const void *p) {
                : "=r"(v.x), "=r"(v.y)
                : "l"(p));
   return v;
+}
+
+// Reads of the L2-coherent copy that the compiler may neither cache nor hoist (polling loops).
+__device__ __forceinline__ uint4 ld_poll_u4(const void *p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ uint2 ld_poll_u2(const void *p) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned ld_poll_u32(const void *p) {
+  unsigned v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Read-only data shared by several warps of a CTA (L1-allocating, non-coherent path).
+__device__ __forceinline__ uint4 ldg_u4(const void *p) {
+  return __ldg(reinterpret_cast<const uint4 *>(p));
+}
+__device__ __forceinline__ uint2 ldg_u2(const void *p) {
+  return __ldg(reinterpret_cast<const uint2 *>(p));
+}
+
+// ---- tagged inter-stage words --------------------------------------------------------------
+// A bf16 value travels with a 16-bit tag in one 32-bit word, (tag << 16) | bits, so a consumer
+// that sees the expected tag also sees the value: no fence or flag is needed between stages.
+// Tags are derived from the launch epoch and the (layer, write) position and are never 0, so a
+// zeroed or stale buffer never looks ready.
+__device__ __forceinline__ unsigned tag_of(unsigned epoch, int layer, int k) {
+  return (unsigned)(((unsigned long long)epoch * 160ull + (unsigned)(layer * 2 + k)) % 65535ull) + 1u;
+}
+__device__ __forceinline__ unsigned tagged(float v, unsigned tag) {
+  return (tag << 16) | (unsigned)__bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+__device__ __forceinline__ bool tag4_ok(const uint4 &v, unsigned tag) {
+  return (v.x >> 16) == tag && (v.y >> 16) == tag && (v.z >> 16) == tag && (v.w >> 16) == tag;
 }
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
