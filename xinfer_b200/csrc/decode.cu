@@ -42,7 +42,11 @@ constexpr int kHdrBytes = 512;
 constexpr int kResRows = 32;                           // residual rows a CTA owns (<= 32)
 constexpr int kResBytes = XB_MAX_BATCH * kResRows * 4;
 constexpr int kRedFloats = 1024;
-constexpr int kUOffset = kHdrBytes + kResBytes + kRedFloats * 4;  // 5632, 128-aligned
+// RoPE cos/sin of every row's position (bf16 pair per frequency), computed once per launch:
+// the positions are the same for every attention layer of the step.
+constexpr int kRopeFreqs = 64;  // rotary_dim / 2 <= 64
+constexpr int kRopeBytes = XB_MAX_BATCH * kRopeFreqs * 4;
+constexpr int kUOffset = kHdrBytes + kResBytes + kRedFloats * 4 + kRopeBytes;  // 7680, 128-aligned
 constexpr int kSmemLimit = 232448;                     // 227 KB opt-in per CTA
 // layout of the per-CTA float scratch `red` during GEMV stages
 constexpr int RED_RESID = 64;   // [NB][rows of this CTA] residual rows (<= 256)
@@ -91,6 +95,8 @@ constexpr int kTraceStride = 3 * kTraceStages + 8;  // u64 words per CTA
 struct SmemHdr {
   uint64_t full[kMaxSlots];
   uint64_t empty[kMaxSlots];
+  long long ids[XB_MAX_BATCH];
+  long long pos[XB_MAX_BATCH];
   int abort;
   int is_last;
   unsigned epoch;
@@ -383,6 +389,7 @@ template <int NB> struct Consumer {
   const StepParams &p;
   SmemHdr *hdr;
   float *red;     // kRedFloats scratch, reused stage by stage
+  unsigned *rope; // [XB_MAX_BATCH][kRopeFreqs] bf16 (cos | sin << 16) of each row's position
   float *hres;    // [NB][kResRows] this CTA's rows of the residual stream, kept across stages
   char *U;        // union region: GEMV activations / attention scratch
   char *ring;
@@ -398,12 +405,25 @@ template <int NB> struct Consumer {
   float am_v = -INFINITY;
   int am_i = 0x7fffffff;
 
-  __device__ Consumer(const StepParams &p_, SmemHdr *h, float *r, float *hr, char *u, char *rg)
-      : p(p_), hdr(h), red(r), hres(hr), U(u), ring(rg) {
+  __device__ Consumer(const StepParams &p_, SmemHdr *h, float *r, unsigned *rp, float *hr, char *u,
+                      char *rg)
+      : p(p_), hdr(h), red(r), rope(rp), hres(hr), U(u), ring(rg) {
     tid = threadIdx.x;
     warp = tid >> 5;
     lane = tid & 31;
     epoch = hdr->epoch;
+  }
+
+  // cos/sin of (float)pos * inv_freq[f] for every row and frequency, rounded to bf16 as the
+  // reference's rotary tables (same fp32 angle and functions as a per-layer evaluation).
+  __device__ void rope_table() {
+    const int nf = p.RD / 2;
+    for (int i = tid; i < p.B * nf; i += kCT) {
+      const int b = i / nf, f = i % nf;
+      const float ang = (float)hdr->pos[b] * p.inv_freq[f];
+      rope[b * kRopeFreqs + f] = pack2(cosf(ang), sinf(ang));
+    }
+    csync();
   }
 
   __device__ __forceinline__ void csync() { named_sync<kCT>(1); }
@@ -450,10 +470,15 @@ template <int NB> struct Consumer {
     if (tr && tid == 0) tr[3 * si] = tr[3 * si + 1] = tr[3 * si + 2] = globaltimer();
     ++sidx;
   }
-  __device__ void trace_mark() {  // end of a GEMV stage's prologue
+  // Stamps of the current stage: [0] begin, [1] inputs ready (end of a GEMV prologue),
+  // [2] weight tiles done.
+  __device__ void trace_mark(int k) {
     if (p.trace && tid == 0) {
       const int si = (sidx - 1) < kTraceStages ? sidx - 1 : kTraceStages - 1;
-      p.trace[(size_t)blockIdx.x * kTraceStride + 3 * si + 2] = globaltimer();
+      unsigned long long *tr = p.trace + (size_t)blockIdx.x * kTraceStride + 3 * si;
+      const unsigned long long t = globaltimer();
+      tr[2] = t;
+      if (k == 1) tr[1] = t;
     }
   }
   __device__ void trace_end() {
@@ -505,7 +530,7 @@ template <int NB> struct Consumer {
         wv[i] = c < nc ? ldnc_u4(w + c * 8) : make_uint4(0, 0, 0, 0);
 #pragma unroll
         for (int b = 0; b < NB; ++b)
-          xv[b][i] = (c < nc && b < p.B) ? ldnc_u4(p.embed + (size_t)token_id(p, b) * H + c * 8)
+          xv[b][i] = (c < nc && b < p.B) ? ldnc_u4(p.embed + (size_t)hdr->ids[b] * H + c * 8)
                                           : make_uint4(0, 0, 0, 0);
       }
     } else {
@@ -675,7 +700,7 @@ template <int NB> struct Consumer {
     const int n = hi - lo;
     for (int i = tid; i < NB * n; i += kCT) {
       const int b = i / n, r = i % n;
-      hres[b * kResRows + r] = b < p.B ? bf(p.embed[(size_t)token_id(p, b) * p.H + lo + r]) : 0.f;
+      hres[b * kResRows + r] = b < p.B ? bf(p.embed[(size_t)hdr->ids[b] * p.H + lo + r]) : 0.f;
     }
   }
 
@@ -730,7 +755,7 @@ template <int NB> struct Consumer {
     // still read them: after the csync above, this CTA has observed every head's core output,
     // which each item writes after its last read of the old window.
     if (stage == ST_OUT_DELTA) conv_state_update(l, tag(l, 0));
-    trace_mark();
+    trace_mark(1);
     switch (epi) {
     case EPI_STORE: tile_loop<false, EPI_STORE>(g, lo, hi, otag); break;
     case EPI_RESID: tile_loop<false, EPI_RESID>(g, lo, hi, otag); break;
@@ -1090,7 +1115,7 @@ template <int NB> struct Consumer {
       const int s = item % splits;
       if (p.q_len[b] == 0) continue;
       const int kvl = p.kv_len[b];
-      const long long pos = position(p, b);
+      const long long pos = hdr->pos[b];
       const int chunk = (kvl + splits - 1) / splits;
       const int j0 = min(kvl, s * chunk), j1 = min(kvl, j0 + chunk);
       const unsigned *x = p.proj + (size_t)b * p.pstride;
@@ -1122,15 +1147,13 @@ template <int NB> struct Consumer {
           }
         __syncwarp();
         const int half = RD / 2;
-        const float fpos = (float)pos;
 #pragma unroll
         for (int e = 0; e < 8; ++e)
           if (e < EPL) {
             const int d = lane * EPL + e;
             if (d < RD) {
-              const int fi = d < half ? d : d - half;
-              const float ang = fpos * p.inv_freq[fi];
-              const float cs = rbf(cosf(ang)), sn = rbf(sinf(ang));
+              const unsigned cw = rope[b * kRopeFreqs + (d < half ? d : d - half)];
+              const float cs = bf_lo(cw), sn = bf_hi(cw);
               const float rot = d < half ? -dst[d + half] : dst[d - half];
               v[e] = rbf(rbf(v[e] * cs) + rbf(rot * sn));
             }
@@ -1350,6 +1373,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   SmemHdr *hdr = reinterpret_cast<SmemHdr *>(smem);
   float *hres = reinterpret_cast<float *>(smem + kHdrBytes);
   float *red = reinterpret_cast<float *>(smem + kHdrBytes + kResBytes);
+  unsigned *rope = reinterpret_cast<unsigned *>(smem + kHdrBytes + kResBytes + kRedFloats * 4);
   char *U = smem + kUOffset;
   char *ring = U + p.ubytes;
   if (threadIdx.x == 0) {
@@ -1363,9 +1387,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     mbar_fence_init();
   }
   // validate token ids once (out-of-range ids are recorded and read as id 0 nowhere: abort)
-  __syncthreads();
-  if (threadIdx.x < p.B) {
-    const long long id = token_id(p, threadIdx.x);
+  if (threadIdx.x < XB_MAX_BATCH) {
+    const int b = threadIdx.x;
+    const long long id = b < p.B ? token_id(p, b) : 0;
+    hdr->ids[b] = id;
+    hdr->pos[b] = b < p.B ? position(p, b) : 0;
     if (id < 0 || id >= p.V) atomicCAS(p.ctrl + CTL_ERR, 0u, (unsigned)DERR_TOKEN);
   }
   __syncthreads();
@@ -1395,7 +1421,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       }
     }
   } else if (!bad) {
-    Consumer<NB> c(p, hdr, red, hres, U, ring);
+    Consumer<NB> c(p, hdr, red, rope, hres, U, ring);
+    c.rope_table();
     walk_step(p, c);
     c.trace_end();
   }
@@ -1478,8 +1505,8 @@ static int check_geometry(const XbGeometry &g) {
   if (G > 4) return fail(XB_ERR_UNSUPPORTED, "at most 4 query heads per KV head");
   if (g.head_dim != 128 && g.head_dim != 256)
     return fail(XB_ERR_UNSUPPORTED, "head_dim must be 128 or 256");
-  if (g.rotary_dim < 2 || g.rotary_dim > g.head_dim || g.rotary_dim % 2)
-    return fail(XB_ERR_INVALID, "invalid rotary_dim");
+  if (g.rotary_dim < 2 || g.rotary_dim > g.head_dim || g.rotary_dim % 2 || g.rotary_dim > 2 * kRopeFreqs)
+    return fail(XB_ERR_INVALID, "invalid rotary_dim (even, <= head_dim and <= 128)");
   if (g.capacity < 1) return fail(XB_ERR_INVALID, "capacity must be positive");
   if (g.state_rows < 1 || g.state_rows > XB_MAX_BATCH)
     return fail(XB_ERR_INVALID, "state_rows must be 1..8");
