@@ -34,7 +34,6 @@ import torch  # noqa: E402
 
 METRIC = "decode tok/s at batch 1 (Qwen3.5-0.8B, 4K ctx); % of HBM roofline"
 UNIT = "tokens/s"
-WORKLOAD = "qwen3.5-0.8b decode, batch 1, 512-token random prompt, 4096-slot capacity"
 PROFILE = ROOT / "profiles" / "decode_megakernel_qwen3.5-0.8b.md"
 
 
@@ -51,6 +50,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--trace", help="save a per-CTA stage trace of one extra step to this file")
     return ap.parse_args()
+
+
+def workload(args):
+    return (f"{args.config} decode, batch 1 per GPU, {args.prompt}-token random prompt, "
+            f"{args.capacity}-slot capacity")
 
 
 def algorithmic_bytes(g, context):
@@ -85,16 +89,25 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
-def traffic_from_profile():
-    if not PROFILE.exists():
+def traffic_from_profile(g, context):
+    """DRAM bytes per launch from the committed ncu capture (dram__bytes_read.sum +
+    dram__bytes_write.sum), moved from the captured KV length to this run's mean context by the
+    KV bytes of the attention layers (the only traffic that depends on the context)."""
+    if not PROFILE.exists() or g.name != "qwen3.5-0.8b":
         return None
+    fields = {}
     for line in PROFILE.read_text().splitlines():
-        if line.strip().startswith("traffic_bytes_per_launch:"):
+        key, _, rest = line.strip().partition(":")
+        if key in ("traffic_bytes_per_launch", "traffic_kv_len") and rest.strip():
             try:
-                return float(line.split(":", 1)[1].split()[0])
+                fields[key] = float(rest.split()[0])
             except ValueError:
                 return None
-    return None
+    if len(fields) != 2:
+        return None
+    n_attn = sum(not g.is_delta(i) for i in range(g.num_layers))
+    kv_token = 2 * g.num_kv_heads * g.head_dim * 2
+    return fields["traffic_bytes_per_launch"] + n_attn * kv_token * (context + 1 - fields["traffic_kv_len"])
 
 
 class Clocks:
@@ -191,7 +204,7 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / res["value"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "impl": "reference",
-        "config": {"workload": WORKLOAD + " (CPU sample)", "model": args.config, "global_batch": 1,
+        "config": {"workload": workload(args) + " (CPU sample)", "model": args.config, "global_batch": 1,
                    "seq_len": args.capacity, "parallelism": "cpu"},
         "cpu_baseline": res,
         "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -306,12 +319,12 @@ def main():
     alg = algorithmic_bytes(g, ctx_mean)
     peak, peak_kind = measured_peak()
     achieved = alg / mean_launch_s / 1e9
-    traffic = traffic_from_profile()
+    traffic = traffic_from_profile(g, ctx_mean)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "model": args.config, "global_batch": world,
+        "config": {"workload": workload(args), "model": args.config, "global_batch": world,
                    "seq_len": args.capacity, "prompt": args.prompt,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (1.5 GB of weights per step)"},
