@@ -464,6 +464,42 @@ template <int NB> struct Consumer {
     return (v.y == tg && v.w == tg) ? v : repoll2f(w, tg, abort_flag(), p.ctrl);
   }
 
+  // Completes a batch of tagged loads: words v[i] with want(i) that are not ok() yet are loaded
+  // again, all of them back to back, until every one is ready, so a late batch costs one L2
+  // round trip per round instead of one per word. addr(i) is word i's address.
+  template <int N, class Addr, class Want, class Ok>
+  __device__ __forceinline__ void settle(uint4 (&v)[N], Addr addr, Want want, Ok ok) const {
+    bool late = false;
+#pragma unroll
+    for (int i = 0; i < N; ++i) late |= want(i) && !ok(v[i]);
+    uint64_t t0 = 0;
+    for (unsigned round = 1; late; ++round) {
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+        if (want(i) && !ok(v[i])) v[i] = ld_poll_u4(addr(i));
+      late = false;
+#pragma unroll
+      for (int i = 0; i < N; ++i) late |= want(i) && !ok(v[i]);
+      if (late && (round & 15u) == 0 && give_up(t0)) break;
+    }
+  }
+  template <int N, class Addr, class Want>
+  __device__ __forceinline__ void settle1(unsigned (&v)[N], Addr addr, Want want, unsigned tg) const {
+    bool late = false;
+#pragma unroll
+    for (int i = 0; i < N; ++i) late |= want(i) && (v[i] >> 16) != tg;
+    uint64_t t0 = 0;
+    for (unsigned round = 1; late; ++round) {
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+        if (want(i) && (v[i] >> 16) != tg) v[i] = ld_poll_u32(addr(i));
+      late = false;
+#pragma unroll
+      for (int i = 0; i < N; ++i) late |= want(i) && (v[i] >> 16) != tg;
+      if (late && (round & 15u) == 0 && give_up(t0)) break;
+    }
+  }
+
   __device__ void stage_begin() {
     unsigned long long *tr = p.trace ? p.trace + (size_t)blockIdx.x * kTraceStride : nullptr;
     const int si = sidx < kTraceStages ? sidx : kTraceStages - 1;
@@ -1010,9 +1046,16 @@ template <int NB> struct Consumer {
         if (lane == 2) gsc = bf(((const bf16 *)w.dt_bias)[h]);
         else if (lane == 3) gsc = bf(((const bf16 *)w.a_log)[h]);
       }
-      const float xq = bf_lo(poll1(x + chq, tg));
-      const float xv = tid < 16 ? bf_lo(poll1(x + chv, tg)) : 0.f;
-      if (warp == 0 && lane < 2) gsc = bf_lo(poll1(x + CH + HV * DK + lane * HV + h, tg));  // b, a
+      // q/k channel, v channel (tid < 16), then b and a (warp 0, lanes 0 and 1), polled together
+      unsigned xw[3];
+      auto xaddr = [&](int k) { return k == 0 ? x + chq : k == 1 ? x + chv : x + CH + HV * DK + lane * HV + h; };
+      auto xwant = [&](int k) { return k == 0 || (k == 1 && tid < 16) || (k == 2 && warp == 0 && lane < 2); };
+#pragma unroll
+      for (int k = 0; k < 3; ++k) xw[k] = xwant(k) ? ld_poll_u32(xaddr(k)) : 0u;
+      settle1(xw, xaddr, xwant, tg);
+      const float xq = bf_lo(xw[0]);
+      const float xv = tid < 16 ? bf_lo(xw[1]) : 0.f;
+      if (warp == 0 && lane < 2) gsc = bf_lo(xw[2]);  // b, a
       // causal conv (width 4) over [conv[1..3], x] + SiLU, rounded as recurrent.py:32-58
       auto conv = [](uint2 cs, uint2 ws, float xx) -> float {
         float tot = 0.f;
