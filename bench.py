@@ -52,6 +52,20 @@ def parse():
     return ap.parse_args()
 
 
+def max_over_ranks(x, dist, device):
+    """The slowest replica's figure: a job of independent replicas ends with its slowest rank."""
+    if dist is None:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_throughput(world, steps, seconds):
+    """Tokens per second of the whole job: each of `world` replicas decodes `steps` tokens."""
+    return world * steps / seconds
+
+
 def workload(args):
     return (f"{args.config} decode, batch 1 per GPU, {args.prompt}-token random prompt, "
             f"{args.capacity}-slot capacity")
@@ -275,11 +289,8 @@ def main():
         barrier()
     ms = ev0.elapsed_time(ev1)
     eng.check_device_error()
-    if dist is not None:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = world * args.steps / (ms / 1000.0)
+    ms = max_over_ranks(ms, dist, dev)
+    value = job_throughput(world, args.steps, ms / 1000.0)
     mean_launch_s = ms / 1000.0 / args.steps
 
     # ---- e2e: public runner path with host buffers -------------------------------------------
@@ -309,11 +320,8 @@ def main():
     e2e_s = time.perf_counter() - t0
     eng.check_device_error()
     barrier()
-    if dist is not None:
-        t = torch.tensor([e2e_s], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e_value = world * args.steps / e2e_s
+    e2e_s = max_over_ranks(e2e_s, dist, dev)
+    e2e_value = job_throughput(world, args.steps, e2e_s)
 
     ctx_mean = start + args.warmup + (args.steps + 1) / 2.0
     alg = algorithmic_bytes(g, ctx_mean)

@@ -160,6 +160,16 @@ int xb_rope_inv_freq(float theta, int32_t rotary_dim, float *out);
  * producer's busy time, its total wait for free slots and the number of tiles it issued. Pass NULL to switch tracing off. The buffer must hold 1024 CTAs' worth. */
 int xb_debug_trace(void *device_buffer, size_t bytes);
 
+/* Fault injection for tests of the bounded waits (the reference's failure handling is the
+ * runner's exception path, runtime/common/runner.h, with no device-side counterpart). For the
+ * launches that follow on the current device: CTA 0 does not publish the outputs of GEMV stage
+ * `withhold_stage` (index in the step's stage order; negative: none), and every wait gives up
+ * after `wait_limit_ns` (0: the default 2 s; at least 1 ms). A withheld stage makes the stages
+ * that read it time out: the launch ends, every CTA returns, and xb_workspace_check reports
+ * XB_ERR_DEVICE with DERR_WAIT (1). xb_debug_fault(-1, 0) restores normal operation. Not for
+ * use while other launches of this library run. */
+int xb_debug_fault(int32_t withhold_stage, uint64_t wait_limit_ns);
+
 const char *xb_last_error(void);
 int xb_abi_version(void);
 

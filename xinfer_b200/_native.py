@@ -22,7 +22,7 @@ LIBRARY_PATH = Path(__file__).resolve().parent / LIBRARY_NAME
 EXPORTED = (
     "xb_model_create", "xb_model_destroy", "xb_decode_workspace_bytes", "xb_workspace_init",
     "xb_decode_step", "xb_workspace_check", "xb_rope_inv_freq", "xb_last_error",
-    "xb_abi_version", "xb_decode_step_static", "xb_debug_trace",
+    "xb_abi_version", "xb_decode_step_static", "xb_debug_trace", "xb_debug_fault",
 )
 TRACE_STAGES = 512
 TRACE_STRIDE = 3 * TRACE_STAGES + 8
@@ -123,6 +123,7 @@ def load():
         "xb_decode_step_static": (i32, [ctypes.POINTER(XbGeometry), ctypes.POINTER(XbModelWeights),
                                         ctypes.POINTER(XbStepArgs), vp, ctypes.POINTER(i32)]),
         "xb_debug_trace": (i32, [vp, sz]),
+        "xb_debug_fault": (i32, [i32, ctypes.c_uint64]),
         "xb_last_error": (ctypes.c_char_p, []),
         "xb_abi_version": (i32, []),
     }

@@ -59,6 +59,11 @@ enum { CTL_ERR = 64, CTL_DONE = 96, CTL_WORDS = 128, CTL_EPOCH = 128, CTL_TOTAL 
 // device error codes
 enum { DERR_WAIT = 1, DERR_RING_FULL = 2, DERR_RING_EMPTY = 3, DERR_TOKEN = 4, DERR_DRAIN = 5 };
 
+// Fault injection for tests of the bounded waits (xb_debug_fault): the wait limit, and a stage
+// (index in the step's stage order) whose outputs CTA 0 does not publish. Defaults: 2 s, none.
+__constant__ unsigned long long c_wait_limit_ns = kWaitLimitNs;
+__constant__ int c_withhold_stage = -1;
+
 enum Stage {
   ST_IN_DELTA = 0, ST_OUT_DELTA, ST_QKV, ST_O, ST_GATEUP, ST_DOWN, ST_LMHEAD
 };
@@ -221,7 +226,7 @@ struct Producer {
         if (t0 == 0) t0 = t;
         else if (t - t0 > kSlowWaitNs) {
           if (ld_volatile(p.ctrl + CTL_ERR)) return false;
-          if (t - t0 > 2 * kWaitLimitNs) {
+          if (t - t0 > 2 * c_wait_limit_ns) {
             atomicCAS(p.ctrl + CTL_ERR, 0u, (unsigned)DERR_RING_EMPTY);
             return false;
           }
@@ -330,7 +335,7 @@ __device__ __forceinline__ bool wait_give_up(volatile int *abort_flag, unsigned 
   if (t0 == 0) { t0 = t; return false; }
   if (t - t0 < kSlowWaitNs) return false;
   if (ld_volatile(ctrl + CTL_ERR)) { *abort_flag = 1; return true; }
-  if (t - t0 > kWaitLimitNs) {
+  if (t - t0 > c_wait_limit_ns) {
     atomicCAS(ctrl + CTL_ERR, 0u, (unsigned)DERR_WAIT);
     *abort_flag = 1;
     return true;
@@ -398,6 +403,7 @@ template <int NB> struct Consumer {
   unsigned phase = 0;
   bool h_ready = false;   // residual stream published (false: still the embedding rows)
   int sidx = 0;           // stage counter (trace)
+  bool withhold = false;  // fault injection (xb_debug_fault)
   unsigned epoch;
   unsigned long long full_wait = 0;  // ns waiting for ring slots (trace, tid 0)
   unsigned long long poll_wait = 0;  // ns waiting for tagged inputs (trace, tid 0)
@@ -504,6 +510,7 @@ template <int NB> struct Consumer {
     unsigned long long *tr = p.trace ? p.trace + (size_t)blockIdx.x * kTraceStride : nullptr;
     const int si = sidx < kTraceStages ? sidx : kTraceStages - 1;
     if (tr && tid == 0) tr[3 * si] = tr[3 * si + 1] = tr[3 * si + 2] = globaltimer();
+    withhold = blockIdx.x == 0 && sidx == c_withhold_stage;
     ++sidx;
   }
   // Stamps of the current stage: [0] begin, [1] inputs ready (end of a GEMV prologue),
@@ -901,6 +908,7 @@ template <int NB> struct Consumer {
 
   __device__ __forceinline__ void epilogue(int epi, int b, int row, float v, float v2, int lo,
                                            unsigned tg) {
+    if (withhold) return;  // fault injection: this stage's outputs of CTA 0 never appear
     switch (epi) {
     case EPI_STORE:
       p.proj[(size_t)b * p.pstride + row] = tagged(v, tg);
@@ -1456,7 +1464,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         const unsigned parity = (unsigned)((k / p.nslots) & 1);
         const uint64_t t0 = globaltimer();
         while (!mbar_try_wait(&hdr->full[slot], parity)) {
-          if (globaltimer() - t0 > kWaitLimitNs) {
+          if (globaltimer() - t0 > 2 * c_wait_limit_ns) {
             atomicCAS(p.ctrl + CTL_ERR, 0u, (unsigned)DERR_DRAIN);
             break;
           }
@@ -1618,6 +1626,15 @@ extern "C" {
 
 const char *xb_last_error(void) { return g_err.c_str(); }
 int xb_abi_version(void) { return XB_ABI_VERSION; }
+
+int xb_debug_fault(int32_t withhold_stage, uint64_t wait_limit_ns) {
+  const int stage = withhold_stage < 0 ? -1 : withhold_stage;
+  const unsigned long long limit = wait_limit_ns ? wait_limit_ns : kWaitLimitNs;
+  if (limit < 1000000ull) return fail(XB_ERR_INVALID, "wait limit below 1 ms");
+  XB_CUDA(cudaMemcpyToSymbol(c_withhold_stage, &stage, sizeof(stage)));
+  XB_CUDA(cudaMemcpyToSymbol(c_wait_limit_ns, &limit, sizeof(limit)));
+  return XB_OK;
+}
 
 int xb_debug_trace(void *device_buffer, size_t bytes) {
   const size_t need = (size_t)kTraceStride * 8 * 1024;
