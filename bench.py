@@ -44,7 +44,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", default="qwen3.5-0.8b")
-    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--prompt", type=int, default=512,
+                    help="prompt length (batch > 1: the largest of the rows' random lengths)")
+    ap.add_argument("--batch", type=int, default=1, help="rows per GPU, 1..8, ragged prompts")
     ap.add_argument("--capacity", type=int, default=4096)
     ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -67,15 +69,19 @@ def job_throughput(world, steps, seconds):
 
 
 def workload(args):
-    return (f"{args.config} decode, batch 1 per GPU, {args.prompt}-token random prompt, "
-            f"{args.capacity}-slot capacity")
+    rows = (f"batch 1, {args.prompt}-token random prompt" if args.batch == 1 else
+            f"batch {args.batch} ragged rows, prompts U[2,{args.prompt}]")
+    return f"{args.config} decode, {rows} per GPU, {args.capacity}-slot capacity"
 
 
-def algorithmic_bytes(g, context):
-    """Bytes one decode token must move: every weight once (tied lm_head counted once, embedding
-    row excluded), recurrent + conv state read and written, KV prefix read plus one slot written."""
+def algorithmic_bytes(g, contexts):
+    """Bytes one decode step must move: every weight once (tied lm_head counted once, embedding
+    rows excluded), then per active row its recurrent + conv state read and written, its KV prefix
+    read plus one slot written. `contexts`: cached positions per row (a number for one row)."""
     from xinfer_b200 import synthetic
 
+    if not isinstance(contexts, (list, tuple)):
+        contexts = [contexts]
     total = 0
     for name, (shape, _) in synthetic.parameter_shapes(g).items():
         if name == "model.embed_tokens.weight":
@@ -89,9 +95,10 @@ def algorithmic_bytes(g, context):
     n_attn = g.num_layers - n_delta
     rec = g.lin_value_heads * g.lin_head_dim * g.lin_head_dim * 4
     conv = g.conv_channels * g.conv_width * 2
-    total += n_delta * 2 * (rec + conv)
     kv_token = 2 * g.num_kv_heads * g.head_dim * 2
-    total += n_attn * kv_token * (context + 1)
+    for context in contexts:
+        total += n_delta * 2 * (rec + conv)
+        total += n_attn * kv_token * (context + 1)
     return total
 
 
@@ -253,8 +260,16 @@ def main():
     weights = synthetic.make_state_dict(g, seed=0, device=dev)
     eng = Engine(g, weights, capacity=args.capacity, device=dev)
     runner = Runner(eng)
-    prompt = synthetic.random_prompt(g, args.prompt, seed=1000 + rank)
-    if args.prompt + 2 * (args.warmup + args.steps) > args.capacity:
+    B = args.batch
+    if not 1 <= B <= 8:
+        raise SystemExit("--batch must be 1..8")
+    if B == 1:
+        lengths = [args.prompt]
+    else:  # ragged rows: lengths ~ U[2, prompt] from a seed (BASELINE's batched configuration)
+        gen = torch.Generator().manual_seed(4242 + rank)
+        lengths = [int(x) for x in torch.randint(2, args.prompt + 1, (B,), generator=gen)]
+    prompts = [synthetic.random_prompt(g, n, seed=1000 + 17 * b + rank) for b, n in enumerate(lengths)]
+    if max(lengths) + args.warmup + args.steps > args.capacity:  # each leg starts from a fresh prefill
         raise SystemExit("prompt + steps exceed the KV capacity")
     stream = torch.cuda.current_stream(dev)
 
@@ -263,17 +278,22 @@ def main():
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    # ---- value: device-resident greedy decode ------------------------------------------------
-    runner.reset()
-    runner.prefill(prompt)
-    start = args.prompt
+    def prefill_rows():
+        runner.reset()
+        for t in range(max(lengths)):
+            runner.step_batch([[p[t]] if t < len(p) else [] for p in prompts])
+
+    starts = list(lengths)
     total = args.warmup + args.steps
-    tok = [torch.zeros(1, dtype=torch.int64, device=dev) for _ in range(2)]
-    tok[0].copy_(runner.next_tokens[:1])
-    pos = torch.arange(start, start + total, dtype=torch.int64, device=dev)
+
+    # ---- value: device-resident greedy decode ------------------------------------------------
+    prefill_rows()
+    tok = [torch.zeros(B, dtype=torch.int64, device=dev) for _ in range(2)]
+    tok[0].copy_(runner.next_tokens[:B])
+    pos = torch.tensor([[s + k for s in starts] for k in range(total)], dtype=torch.int64, device=dev)
 
     def device_step(k):
-        eng.launch(tok[k % 2], pos[k:k + 1], [start + k + 1], [1], runner.state, runner.state,
+        eng.launch(tok[k % 2], pos[k], [s + k + 1 for s in starts], [1] * B, runner.state, runner.state,
                    runner.logits, tok[(k + 1) % 2])
 
     for k in range(args.warmup):
@@ -290,26 +310,27 @@ def main():
     ms = ev0.elapsed_time(ev1)
     eng.check_device_error()
     ms = max_over_ranks(ms, dist, dev)
-    value = job_throughput(world, args.steps, ms / 1000.0)
+    value = job_throughput(world, B * args.steps, ms / 1000.0)
     mean_launch_s = ms / 1000.0 / args.steps
 
     # ---- e2e: public runner path with host buffers -------------------------------------------
-    runner.reset()
-    runner.prefill(prompt)
-    host_in = torch.zeros(2, dtype=torch.int64).pin_memory()
-    host_out = torch.zeros(1, dtype=torch.int64).pin_memory()
-    dev_in = torch.zeros(2, dtype=torch.int64, device=dev)
-    next_host = runner.next_token()
+    prefill_rows()
+    host_in = torch.zeros(2 * B, dtype=torch.int64).pin_memory()
+    host_out = torch.zeros(B, dtype=torch.int64).pin_memory()
+    dev_in = torch.zeros(2 * B, dtype=torch.int64, device=dev)
+    host_out.copy_(runner.next_tokens[:B])
+    next_host = [int(x) for x in host_out]
 
-    def e2e_step(k, token):
-        host_in[0] = token
-        host_in[1] = start + k
+    def e2e_step(k, tokens):
+        for b in range(B):
+            host_in[b] = tokens[b]
+            host_in[B + b] = starts[b] + k
         dev_in.copy_(host_in, non_blocking=True)
-        eng.launch(dev_in[0:1], dev_in[1:2], [start + k + 1], [1], runner.state, runner.state,
-                   runner.logits, runner.next_tokens)
-        host_out.copy_(runner.next_tokens[:1], non_blocking=True)
+        eng.launch(dev_in[0:B], dev_in[B:2 * B], [s + k + 1 for s in starts], [1] * B, runner.state,
+                   runner.state, runner.logits, runner.next_tokens)
+        host_out.copy_(runner.next_tokens[:B], non_blocking=True)
         stream.synchronize()
-        return int(host_out[0])
+        return [int(x) for x in host_out]
 
     for k in range(args.warmup):
         next_host = e2e_step(k, next_host)
@@ -321,25 +342,26 @@ def main():
     eng.check_device_error()
     barrier()
     e2e_s = max_over_ranks(e2e_s, dist, dev)
-    e2e_value = job_throughput(world, args.steps, e2e_s)
+    e2e_value = job_throughput(world, B * args.steps, e2e_s)
 
-    ctx_mean = start + args.warmup + (args.steps + 1) / 2.0
-    alg = algorithmic_bytes(g, ctx_mean)
+    ctxs = [st + args.warmup + (args.steps + 1) / 2.0 for st in starts]
+    ctx_mean = sum(ctxs) / B
+    alg = algorithmic_bytes(g, ctxs)
     peak, peak_kind = measured_peak()
     achieved = alg / mean_launch_s / 1e9
-    traffic = traffic_from_profile(g, ctx_mean)
+    traffic = traffic_from_profile(g, ctx_mean) if B == 1 else None
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": workload(args), "model": args.config, "global_batch": world,
+        "config": {"workload": workload(args), "model": args.config, "global_batch": world * B,
                    "seq_len": args.capacity, "prompt": args.prompt,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (1.5 GB of weights per step)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": alg, "traffic": traffic},
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 8},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 16 * B, "d2h_bytes_per_step": 8 * B},
         "gpu_launches": args.steps,
         "clocks": clocks.summary(),
     }
@@ -349,7 +371,7 @@ def main():
         buf = torch.zeros(nat.TRACE_BYTES // 8, dtype=torch.int64, device=dev)
         nat.check(nat.load().xb_debug_trace(buf.data_ptr(), nat.TRACE_BYTES))
         runner.reset()
-        runner.prefill(prompt[:64])
+        runner.prefill(prompts[0][:64])
         torch.cuda.synchronize(dev)
         nat.check(nat.load().xb_debug_trace(None, 0))
         torch.save({"trace": buf.cpu(), "ncta": torch.cuda.get_device_properties(dev).multi_processor_count,

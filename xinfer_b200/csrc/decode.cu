@@ -49,8 +49,7 @@ constexpr int kRopeBytes = XB_MAX_BATCH * kRopeFreqs * 4;
 constexpr int kUOffset = kHdrBytes + kResBytes + kRedFloats * 4 + kRopeBytes;  // 7680, 128-aligned
 constexpr int kSmemLimit = 232448;                     // 227 KB opt-in per CTA
 // layout of the per-CTA float scratch `red` during GEMV stages
-constexpr int RED_RESID = 64;   // [NB][rows of this CTA] residual rows (<= 256)
-constexpr int RED_PART = 512;   // [2][kWarps][2][NB][2] split-K partials
+constexpr int RED_PART = 512;   // [2][kWarps][2][NB][2] split-K partials (batch 1 tiles)
 
 // control words in the workspace (each on its own 128-byte line)
 // Words [0, CTL_WORDS) are cleared whenever a workspace is reset; the launch epoch (which
@@ -129,6 +128,13 @@ __device__ __forceinline__ long long position(const StepParams &p, int b) {
 __device__ __forceinline__ bool is_delta(const StepParams &p, int l) {
   return (p.delta_mask >> l) & 1ull;
 }
+// Stage [src, src + bytes) from global memory into L2 (16-byte aligned, multiple of 16 bytes).
+__device__ __forceinline__ void prefetch_l2(const void *src, size_t bytes) {
+  for (size_t o = 0; o < bytes; o += 65536)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((const char *)src + o),
+                 "r"((unsigned)(bytes - o < 65536 ? bytes - o : 65536))
+                 : "memory");
+}
 
 __device__ __forceinline__ Gemv make_gemv(const StepParams &p, int l, int stage) {
   Gemv g;
@@ -183,8 +189,11 @@ __device__ __forceinline__ Gemv make_gemv(const StepParams &p, int l, int stage)
   return g;
 }
 
-__device__ __forceinline__ int tile_rows(const Gemv &g) {
-  return kSlot / (g.K * 2 * (g.paired ? 2 : 1));
+// Rows of one ring tile. With padding (batch >= 4, tensor-core tiles of 16 rows) every row
+// occupies K * 2 + 16 bytes so that the 8 rows one MMA fragment reads fall in different banks.
+__device__ __forceinline__ int tile_rows(const Gemv &g, bool pad) {
+  const int r = kSlot / ((g.K * 2 + (pad ? 16 : 0)) * (g.paired ? 2 : 1));
+  return pad ? min(r, g.paired ? 8 : 16) : r;
 }
 __device__ __forceinline__ void cta_range(int N, int cta, int ncta, int &lo, int &hi) {
   lo = (int)(((long long)N * cta) / ncta);
@@ -194,7 +203,7 @@ __device__ __forceinline__ void cta_range(int N, int cta, int ncta, int &lo, int
 // ------------------------------------------------------------------------------------------
 // Producer role: lane 0 of the last warp issues every weight tile of this CTA, in order.
 // ------------------------------------------------------------------------------------------
-struct Producer {
+template <bool PAD> struct Producer {
   const StepParams &p;
   SmemHdr *hdr;
   char *ring;
@@ -241,14 +250,30 @@ struct Producer {
     const Gemv g = make_gemv(p, l, stage);
     int lo, hi;
     cta_range(g.N, blockIdx.x, p.ncta, lo, hi);
-    const int R = tile_rows(g);
+    const int R = tile_rows(g, PAD);
     const unsigned rowb = (unsigned)g.K * 2u;
     for (int r0 = lo; r0 < hi; r0 += R) {
       const int n = min(R, hi - r0);
       if (!acquire()) { stop = true; return; }
       char *dst = ring + (size_t)slot * kSlot;
       uint64_t *bar = &hdr->full[slot];
-      if (g.paired) {
+      if (PAD) {
+        // one copy per row into a padded row slot: gate/up tiles hold n gate rows, then n up rows
+        const unsigned pitch = rowb + 16u;
+        mbar_arrive_expect_tx(bar, (unsigned)n * rowb * (g.paired ? 2u : 1u));
+        if (g.paired) {
+          for (int r = 0; r < n; ++r) {
+            bulk_g2s(dst + (size_t)r * pitch, g.seg[0] + (size_t)(r0 + r) * g.K, rowb, bar, policy);
+            bulk_g2s(dst + (size_t)(n + r) * pitch, g.seg[1] + (size_t)(r0 + r) * g.K, rowb, bar, policy);
+          }
+        } else {
+          int sg = 0, base = 0;
+          for (int r = 0; r < n; ++r) {
+            while (sg + 1 < g.nseg && r0 + r >= base + g.seg_rows[sg]) base += g.seg_rows[sg++];
+            bulk_g2s(dst + (size_t)r * pitch, g.seg[sg] + (size_t)(r0 + r - base) * g.K, rowb, bar, policy);
+          }
+        }
+      } else if (g.paired) {
         const unsigned bytes = (unsigned)n * rowb;
         mbar_arrive_expect_tx(bar, 2u * bytes);
         bulk_g2s(dst, g.seg[0] + (size_t)r0 * g.K, bytes, bar, policy);
@@ -325,6 +350,16 @@ __device__ __forceinline__ float2 gemv_pair(const uint4 *__restrict__ wA, const 
 }
 
 
+// D += A (16 x 16, row-major) * B (16 x 8, column-major), bf16 inputs, fp32 accumulation.
+__device__ __forceinline__ void mma_16816(float (&d)[4], unsigned a0, unsigned a1, unsigned a2,
+                                          unsigned a3, unsigned b0, unsigned b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // ---- waits (free functions: the consumer object must never have its address taken, so that
 // its state stays in registers) -------------------------------------------------------------
 // True when a wait must end: this CTA aborted, or (only after kSlowWaitNs of waiting, so that the
@@ -391,6 +426,7 @@ __device__ __noinline__ float repoll1f(const uint2 *w, unsigned tg, volatile int
 // Consumer role
 // ------------------------------------------------------------------------------------------
 template <int NB> struct Consumer {
+  static constexpr int kPad = NB >= 4 ? 1 : 0;  // padded rows (tensor-core tiles)
   const StepParams &p;
   SmemHdr *hdr;
   float *red;     // kRedFloats scratch, reused stage by stage
@@ -410,6 +446,7 @@ template <int NB> struct Consumer {
   // running argmax for the lm_head stage (lane b / 16 + b keeps batch row b)
   float am_v = -INFINITY;
   int am_i = 0x7fffffff;
+  int am_b = -1;  // batch row whose logits this thread reduced
 
   __device__ Consumer(const StepParams &p_, SmemHdr *h, float *r, unsigned *rp, float *hr, char *u,
                       char *rg)
@@ -638,7 +675,7 @@ template <int NB> struct Consumer {
 #pragma unroll
         for (int e = 0; e < 8; ++e)
           y[e] = (b < p.B) ? (q35 ? x[e] * r * (1.f + wf[e]) : wf[e] * rbf(x[e] * r)) : 0.f;
-        act[b * nc + c] = make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]),
+        act[b * (nc + kPad) + c] = make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]),
                                      pack2(y[6], y[7]));
       }
     }
@@ -666,7 +703,7 @@ template <int NB> struct Consumer {
           const uint4 q = check4(src + (size_t)b * ld + c * 4, v[i], tg);
           o = make_uint2((q.x & 0xffffu) | (q.y << 16), (q.z & 0xffffu) | (q.w << 16));
         }
-        act[b * nq + c] = o;
+        act[b * (nq + 2 * kPad) + c] = o;
       }
     }
   }
@@ -711,7 +748,7 @@ template <int NB> struct Consumer {
           }
           o = make_uint2(pack2(y[0], y[1]), pack2(y[2], y[3]));
         }
-        act[b * nq + c] = o;
+        act[b * (nq + 2 * kPad) + c] = o;
       }
     }
   }
@@ -817,8 +854,69 @@ template <int NB> struct Consumer {
   // over S warps per pair and combine the partial sums in shared memory.
   template <bool PAIRED, int EPI>
   __device__ __forceinline__ void tile_loop(const Gemv &g, int lo, int hi, unsigned otag) {
+    if constexpr (NB >= 4) tile_loop_mma<PAIRED>(g, lo, hi, otag, EPI);
+    else tile_loop_fma<PAIRED, EPI>(g, lo, hi, otag);
+  }
+
+  // Batch rows 4..8: tensor-core tiles. A tile's rows (gate/up tiles: n gate rows, then n up
+  // rows) form one 16-row block; warp w multiplies it by the activations over the w-th eighth of
+  // K with m16n8k16 MMAs (rows as M, batch rows as N, missing rows and batch rows as zeros) and
+  // the eight partial blocks are summed in a fixed order through shared memory. Rows in shared
+  // memory are padded to K * 2 + 16 bytes, so the fragment loads are free of bank conflicts. The
+  // K order inside a block is permuted identically for A and B (lane t of a row group reads the
+  // four contiguous values 4t..4t+3), which leaves each dot product unchanged.
+  template <bool PAIRED>
+  __device__ __forceinline__ void tile_loop_mma(const Gemv &g, int lo, int hi, unsigned otag, int epi) {
+    const int pitch = g.K * 2 + 16;
+    const int R = tile_rows(g, true);
+    const int nkb = g.K / 16;
+    const int kb0 = nkb * warp / kWarps, kb1 = nkb * (warp + 1) / kWarps;
+    const int gq = lane >> 2, t4 = lane & 3;
+    const char *xrow = U + (size_t)gq * pitch;  // activations of batch row gq
+    const bool xok = gq < NB;
+    for (int r0 = lo; r0 < hi; r0 += R) {
+      const int n = min(R, hi - r0);
+      const int rows = PAIRED ? 2 * n : n;
+      const char *slotp = wait_full();
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      if (slotp) {
+        const bool okA = gq < rows, okB = gq + 8 < rows;
+        const char *pa = slotp + (size_t)gq * pitch, *pb = slotp + (size_t)(gq + 8) * pitch;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          const int ko = kb * 32 + t4 * 8;
+          const uint2 a = okA ? *reinterpret_cast<const uint2 *>(pa + ko) : make_uint2(0, 0);
+          const uint2 c = okB ? *reinterpret_cast<const uint2 *>(pb + ko) : make_uint2(0, 0);
+          const uint2 x = xok ? *reinterpret_cast<const uint2 *>(xrow + ko) : make_uint2(0, 0);
+          mma_16816(d, a.x, c.x, a.y, c.y, x.x, x.y);
+        }
+      }
+      float *pw = red + warp * 128;  // [16 rows][8 batch rows]
+      pw[gq * 8 + 2 * t4] = d[0];
+      pw[gq * 8 + 2 * t4 + 1] = d[1];
+      pw[(gq + 8) * 8 + 2 * t4] = d[2];
+      pw[(gq + 8) * 8 + 2 * t4 + 1] = d[3];
+      release();
+      csync();
+      if (slotp && tid < 128) {
+        const int r = tid >> 3, b = tid & 7;
+        if (r < n && b < p.B) {
+          float v = 0.f, v2 = 0.f;
+#pragma unroll
+          for (int w = 0; w < kWarps; ++w) v += red[w * 128 + r * 8 + b];
+          if (PAIRED)
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) v2 += red[w * 128 + (n + r) * 8 + b];
+          epilogue(epi, b, r0 + r, v, v2, lo, otag);
+        }
+      }
+      csync();  // partial sums consumed before the next tile writes them
+    }
+  }
+
+  template <bool PAIRED, int EPI>
+  __device__ __forceinline__ void tile_loop_fma(const Gemv &g, int lo, int hi, unsigned otag) {
     const uint4 *act4 = reinterpret_cast<const uint4 *>(U);
-    const int R = tile_rows(g);
+    const int R = tile_rows(g, false);
     const int K = g.K, n8 = K / 8;
     const size_t rowb = (size_t)K * 2;
     const int bsel = lane & 15;
@@ -929,6 +1027,7 @@ template <int NB> struct Consumer {
     case EPI_LOGITS: {
       const float y = p.q_len[b] > 0 ? rbf(v) : 0.f;
       p.logits[(size_t)b * p.V + row] = tobf(y);
+      am_b = b;
       if (argmax_better(y, row, am_v, am_i)) { am_v = y; am_i = row; }
       break;
     }
@@ -938,22 +1037,31 @@ template <int NB> struct Consumer {
   // Per-CTA argmax -> workspace; the last CTA to finish reduces all CTAs, writes the tokens,
   // advances the launch epoch and resets its own ticket for the next launch.
   __device__ void argmax_finish() {
-    float *sv = red;                                  // [kWarps][2][NB]
-    int *si = reinterpret_cast<int *>(red + 2 * kWarps * NB);
-    const int bsel = lane & 15;
-    if (bsel < NB) {
-      const int k = (warp * 2 + (lane >= 16 ? 1 : 0)) * NB + bsel;
+    // Per-thread candidates: every thread (tensor-core tiles), or the epilogue lanes b and
+    // 16 + b of each warp (batch rows below 4).
+    constexpr int NC = NB >= 4 ? kCT : 2 * kWarps;
+    float *sv = red;
+    int *si = reinterpret_cast<int *>(red + kCT);
+    int *sb = reinterpret_cast<int *>(red + 2 * kCT);
+    csync();  // the lm_head tiles' scratch in red has been consumed
+    if (NB >= 4) {
+      sv[tid] = am_v;
+      si[tid] = am_i;
+      sb[tid] = am_b;
+    } else if ((lane & 15) < NB) {
+      const int k = (warp * 2 + (lane >= 16 ? 1 : 0)) * NB + (lane & 15);
       sv[k] = am_v;
       si[k] = am_i;
+      sb[k] = am_b;
     }
     csync();
     if (tid < NB && tid < p.B) {
       float bv = -INFINITY;
       int bi = 0x7fffffff;
-      for (int k = 0; k < 2 * kWarps; ++k)
-        if (argmax_better(sv[k * NB + tid], si[k * NB + tid], bv, bi)) {
-          bv = sv[k * NB + tid];
-          bi = si[k * NB + tid];
+      for (int k = 0; k < (NB >= 4 ? NC : NC * NB); ++k)
+        if (sb[k] == tid && argmax_better(sv[k], si[k], bv, bi)) {
+          bv = sv[k];
+          bi = si[k];
         }
       p.am_v[blockIdx.x * XB_MAX_BATCH + tid] = bv;
       p.am_i[blockIdx.x * XB_MAX_BATCH + tid] = bi;
@@ -1170,6 +1278,14 @@ template <int NB> struct Consumer {
       const int chunk = (kvl + splits - 1) / splits;
       const int j0 = min(kvl, s * chunk), j1 = min(kvl, j0 + chunk);
       const unsigned *x = p.proj + (size_t)b * p.pstride;
+      bf16 *kc = kc_all + (((size_t)b * HKV + kvh) * p.C) * D;
+      bf16 *vc = vc_all + (((size_t)b * HKV + kvh) * p.C) * D;
+      // Long ranges: this item's K/V rows head for L2 while the query is still being computed
+      // upstream (the position loop keeps too few loads in flight to pull them from HBM itself).
+      if (tid == 0 && j1 - j0 >= 64) {
+        prefetch_l2(kc + (size_t)j0 * D, (size_t)(j1 - j0) * D * 2);
+        prefetch_l2(vc + (size_t)j0 * D, (size_t)(j1 - j0) * D * 2);
+      }
       // warps 0..G-1: query heads; warp G: new key; warp G+1: new value
       if (warp <= G) {
         const bool isk = warp == G;
@@ -1225,8 +1341,6 @@ template <int NB> struct Consumer {
           }
       }
       csync();
-      bf16 *kc = kc_all + (((size_t)b * HKV + kvh) * p.C) * D;
-      bf16 *vc = vc_all + (((size_t)b * HKV + kvh) * p.C) * D;
       // KV append (compiler/common/kernels/kv_cache.py:8-42): the s == 0 item writes slot pos.
       if (s == 0 && pos >= 0 && pos < p.C && tid < D) {
         kc[(size_t)pos * D + tid] = tobf(kn[tid]);
@@ -1449,7 +1563,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
   const bool bad = ld_volatile(p.ctrl + CTL_ERR) != 0;
   if (threadIdx.x >= kCT) {
     if (threadIdx.x == kCT && !bad) {
-      Producer pr(p, hdr, ring);
+      Producer<(NB >= 4)> pr(p, hdr, ring);
       const uint64_t t_start = globaltimer();
       walk_step(p, pr);
       if (p.trace) {
@@ -1589,7 +1703,7 @@ static size_t ubytes_for(const XbGeometry &g, int NB) {
   int kmax = std::max(g.hidden, g.intermediate);
   kmax = std::max(kmax, g.num_q_heads * g.head_dim);
   if (q35) kmax = std::max(kmax, g.lin_value_heads * g.lin_head_dim);
-  const size_t act = (size_t)NB * kmax * 2;
+  const size_t act = (size_t)NB * (kmax * 2 + (NB >= 4 ? 16 : 0));  // padded rows at batch >= 4
   const int G = g.num_q_heads / g.num_kv_heads;
   const size_t att = ((size_t)G * g.head_dim + 2 * g.head_dim + (size_t)kWarps * (g.head_dim + 2)) * 4;
   const size_t u = std::max(act, att);
