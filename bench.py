@@ -319,18 +319,21 @@ def main():
     host_out = torch.zeros(B, dtype=torch.int64).pin_memory()
     dev_in = torch.zeros(2 * B, dtype=torch.int64, device=dev)
     host_out.copy_(runner.next_tokens[:B])
-    next_host = [int(x) for x in host_out]
+    hin, hout = host_in.numpy(), host_out.numpy()  # views of the pinned buffers
+    ids_dev, pos_dev, next_dev = dev_in[0:B], dev_in[B:2 * B], runner.next_tokens[:B]
+    starts_np = hin[B:2 * B].copy()
+    starts_np[:] = starts
+    next_host = hout.copy()
 
     def e2e_step(k, tokens):
-        for b in range(B):
-            host_in[b] = tokens[b]
-            host_in[B + b] = starts[b] + k
+        hin[:B] = tokens
+        hin[B:] = starts_np + k
         dev_in.copy_(host_in, non_blocking=True)
-        eng.launch(dev_in[0:B], dev_in[B:2 * B], [s + k + 1 for s in starts], [1] * B, runner.state,
+        eng.launch(ids_dev, pos_dev, [s + k + 1 for s in starts], [1] * B, runner.state,
                    runner.state, runner.logits, runner.next_tokens)
-        host_out.copy_(runner.next_tokens[:B], non_blocking=True)
+        host_out.copy_(next_dev, non_blocking=True)
         stream.synchronize()
-        return [int(x) for x in host_out]
+        return hout.copy()
 
     for k in range(args.warmup):
         next_host = e2e_step(k, next_host)

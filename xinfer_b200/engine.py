@@ -103,6 +103,8 @@ class Engine:
         nat.check(self.lib.xb_decode_workspace_bytes(handle, nat.MAX_BATCH, ctypes.byref(nbytes)))
         self.workspace = torch.zeros(nbytes.value, dtype=torch.uint8, device=self.device)
         self._args = nat.XbStepArgs()
+        self._ws_ptr, self._ws_bytes = self.workspace.data_ptr(), self.workspace.numel()
+        self._bound_in = self._bound_out = None
 
     def close(self):
         if getattr(self, "handle", None):
@@ -155,6 +157,19 @@ class Engine:
         for b in range(B):
             a.kv_lengths[b] = int(kv_lengths[b])
             a.query_lengths[b] = int(query_lengths[b])
+        if state_in is not self._bound_in or state_out is not self._bound_out:
+            self._bind(state_in, state_out)
+        a.logits = logits.data_ptr()
+        a.next_tokens = next_tokens.data_ptr() if next_tokens is not None else None
+        st = stream if stream is not None else torch.cuda.current_stream(self.device)
+        nat.check(self.lib.xb_decode_step(self.handle, ctypes.byref(a), self._ws_ptr, self._ws_bytes,
+                                          ctypes.c_void_p(st.cuda_stream)))
+
+    def _bind(self, state_in, state_out):
+        """Per-layer state pointers of the launch arguments. They are kept for the next launch
+        with the same two list objects (a decode loop passes its state lists unchanged), so a
+        caller that replaces tensors inside a list must pass a new list."""
+        a = self._args
         for i in range(self.g.num_layers):
             ls = a.layers[i]
             s0, s1 = state_in[2 * i], state_in[2 * i + 1]
@@ -166,11 +181,7 @@ class Engine:
             else:
                 ls.k_cache, ls.v_cache = s0.data_ptr(), s1.data_ptr()
                 ls.conv_in = ls.rec_in = ls.conv_out = ls.rec_out = None
-        a.logits = logits.data_ptr()
-        a.next_tokens = next_tokens.data_ptr() if next_tokens is not None else None
-        st = stream if stream is not None else torch.cuda.current_stream(self.device)
-        nat.check(self.lib.xb_decode_step(self.handle, ctypes.byref(a), self.workspace.data_ptr(),
-                                          self.workspace.numel(), ctypes.c_void_p(st.cuda_stream)))
+        self._bound_in, self._bound_out = state_in, state_out
 
     def check_device_error(self, stream=None):
         st = stream if stream is not None else torch.cuda.current_stream(self.device)
