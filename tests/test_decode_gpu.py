@@ -122,9 +122,11 @@ def schedule_single(g, steps, seed=3):
     return [[[int(torch.randint(0, g.vocab, (1,), generator=gen))]] for _ in range(steps)]
 
 
-def schedule_batch(g, seed=5):
+def schedule_batch(g, seed=5, rows=4):
     gen = torch.Generator().manual_seed(seed)
     active = [(1, 1, 1, 1), (1, 0, 1, 1), (1, 1, 0, 1), (0, 1, 1, 1), (1, 1, 1, 0), (1, 0, 0, 1)]
+    if rows != 4:  # every row starts active, later steps leave some rows empty
+        active = [tuple(1 if s == 0 or (r + s) % 3 else 0 for r in range(rows)) for s in range(6)]
     return [[[int(torch.randint(0, g.vocab, (1,), generator=gen))] if a else [] for a in row]
             for row in active]
 
@@ -168,10 +170,12 @@ def test_full_width_matches_oracle(name, cuda_device):
         assert O.rel_l2(a, b) <= 2 * STATE_REL, f"state {i}"
 
 
+@pytest.mark.parametrize("rows", [4, 8])
 @pytest.mark.parametrize("name", ["qwen3-tiny", "qwen3.5-tiny"])
-def test_ragged_batch_with_empty_rows(name, cuda_device):
+def test_ragged_batch_with_empty_rows(name, rows, cuda_device):
+    """Batch rows 4..8 run the tensor-core GEMV tiles; 2 (below) the FMA tiles."""
     g, sd, W, eng = model(name, 16, cuda_device)
-    sched = schedule_batch(g)
+    sched = schedule_batch(g, rows=rows)
     got, toks, state, full = run_schedule_gpu(eng, g, sched, cuda_device)
     want, ostate = run_schedule_oracle(g, W, sched, 16)
     for s, tokens in enumerate(sched):
@@ -185,6 +189,23 @@ def test_ragged_batch_with_empty_rows(name, cuda_device):
     rows = len(sched[0])
     for t in full:
         assert torch.count_nonzero(t[rows:]) == 0
+
+
+@pytest.mark.parametrize("name,rows", [("qwen3.5-0.8b-l4", 6), ("qwen3-0.6b-l2", 3)])
+def test_full_width_batch_matches_oracle(name, rows, cuda_device):
+    """Tensor-core tiles at real widths (K up to 3584, 248K vocabulary), ragged rows."""
+    g, sd, W, eng = model(name, 16, cuda_device, jitter=0.1)
+    sched = schedule_batch(g, seed=11, rows=rows)[:3]
+    got, toks, state, _ = run_schedule_gpu(eng, g, sched, cuda_device)
+    want, ostate = run_schedule_oracle(g, W, sched, 16)
+    for s, tokens in enumerate(sched):
+        for r, t in enumerate(tokens):
+            if t:
+                check_logits(got[s, r], want[s, r], f"{name} step {s} row {r}", cos_min=FULLW_COS,
+                             max_abs=FULLW_MAX_ABS)
+                assert int(toks[s, r]) == int(torch.argmax(got[s, r].float()))
+            else:
+                assert torch.count_nonzero(got[s, r]) == 0
 
 
 def test_empty_row_keeps_state_bitwise(cuda_device):
