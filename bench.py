@@ -374,7 +374,8 @@ def main():
         buf = torch.zeros(nat.TRACE_BYTES // 8, dtype=torch.int64, device=dev)
         nat.check(nat.load().xb_debug_trace(buf.data_ptr(), nat.TRACE_BYTES))
         runner.reset()
-        runner.prefill(prompts[0][:64])
+        for t in range(min(64, max(lengths))):
+            runner.step_batch([[p_[t]] if t < len(p_) else [] for p_ in prompts])
         torch.cuda.synchronize(dev)
         nat.check(nat.load().xb_debug_trace(None, 0))
         torch.save({"trace": buf.cpu(), "ncta": torch.cuda.get_device_properties(dev).multi_processor_count,

@@ -625,6 +625,7 @@ template <int NB> struct Consumer {
                       (c.x & 0xffffu) | (c.y << 16), (c.z & 0xffffu) | (c.w << 16));
   }
 
+#if !XB_TENSOR_TILES
   // RMSNorm of the residual stream into the activation buffer (bf16 [NB][H]).
   //  Qwen3   : w * bf16(x * rsqrt(mean(x^2) + eps))        (HF Qwen3RMSNorm)
   //  Qwen3.5 : bf16(x * rsqrt(mean(x^2) + eps) * (1 + w))   (HF Qwen3_5RMSNorm)
@@ -710,7 +711,100 @@ template <int NB> struct Consumer {
       }
     }
   }
+#else
+  // RMSNorm of the residual stream for batch rows 4..8 (same formula and summation order as the
+  // small-batch version): two rows' tagged words per round trip, the raw bf16 rows staged in the
+  // (padded) activation rows and normalised there in place.
+  __device__ void norm_prologue(const bf16 *w, unsigned tg) {
+    uint4 *act = reinterpret_cast<uint4 *>(U);
+    const int H = p.H, nc = H / 8, ap = nc + 1;
+    constexpr int MAXC = 2;  // H <= 2 * 256 * 8
+    uint4 wv[MAXC];
+    float ss[NB];
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = tid + i * kCT;
+      wv[i] = c < nc ? ldnc_u4(w + c * 8) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) ss[b] = 0.f;
+    auto sumsq = [&](const uint4 &xv, float acc) {
+      float x[8];
+      unpack8(xv, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc = fmaf(x[e], x[e], acc);
+      return acc;
+    };
+#pragma unroll
+    for (int b0 = 0; b0 < NB; b0 += 2) {
+      if (!h_ready) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int i = 0; i < MAXC; ++i) {
+            const int c = tid + i * kCT, b = b0 + j;
+            if (c >= nc) continue;
+            const uint4 xv = b < p.B ? ldnc_u4(p.embed + (size_t)hdr->ids[b] * H + c * 8) : make_uint4(0, 0, 0, 0);
+            act[b * ap + c] = xv;
+            ss[b] = sumsq(xv, ss[b]);
+          }
+      } else {
+        uint4 u[2 * MAXC * 2];  // (row j, chunk i, half)
+        auto addr = [&](int k) {
+          const int j = k / (2 * MAXC), i = (k / 2) % MAXC;
+          return p.h + (size_t)(b0 + j) * H + (tid + i * kCT) * 8 + (k & 1) * 4;
+        };
+        auto want = [&](int k) {
+          const int j = k / (2 * MAXC), i = (k / 2) % MAXC;
+          return tid + i * kCT < nc && b0 + j < p.B;
+        };
+#pragma unroll
+        for (int k = 0; k < 2 * MAXC * 2; ++k) u[k] = want(k) ? ldcg_u4(addr(k)) : make_uint4(0, 0, 0, 0);
+        settle(u, addr, want, [&](const uint4 &v) { return tag4_ok(v, tg); });
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int i = 0; i < MAXC; ++i) {
+            const int c = tid + i * kCT, b = b0 + j, k = (j * MAXC + i) * 2;
+            if (c >= nc) continue;
+            const uint4 xv = b < p.B ? pack_words(u[k], u[k + 1]) : make_uint4(0, 0, 0, 0);
+            act[b * ap + c] = xv;
+            ss[b] = sumsq(xv, ss[b]);
+          }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      const float t = warp_sum(ss[b]);
+      if (lane == 0) red[warp * NB + b] = t;
+    }
+    csync();
+    const bool q35 = p.family == XB_FAMILY_QWEN35;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      float tot = 0.f;
+#pragma unroll
+      for (int i = 0; i < kWarps; ++i) tot += red[i * NB + b];
+      const float r = rsqrtf(tot / (float)H + p.eps);
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = tid + i * kCT;
+        if (c >= nc) continue;
+        float x[8], wf[8], y[8];
+        unpack8(act[b * ap + c], x);
+        unpack8(wv[i], wf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          y[e] = (b < p.B) ? (q35 ? x[e] * r * (1.f + wf[e]) : wf[e] * rbf(x[e] * r)) : 0.f;
+        act[b * ap + c] = make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]),
+                                     pack2(y[6], y[7]));
+      }
+    }
+  }
 
+#endif
+
+#if !XB_TENSOR_TILES
   // Tagged bf16 vector [B][K] (row stride ld words) into the activations.
   __device__ void copy_prologue(const unsigned *src, int K, int ld, unsigned tg) {
     uint2 *act = reinterpret_cast<uint2 *>(U);  // 4 bf16 per uint2
@@ -737,7 +831,35 @@ template <int NB> struct Consumer {
       }
     }
   }
+#else
+  // Tagged bf16 vectors [B][K] (row stride ld words) into the padded activation rows, batch
+  // rows 4..8: all words of a row in one round trip.
+  __device__ void copy_prologue(const unsigned *src, int K, int ld, unsigned tg) {
+    uint2 *act = reinterpret_cast<uint2 *>(U);  // 4 bf16 per uint2
+    const int nq = K / 4, aq = nq + 2;
+    constexpr int MAXC = 10;  // K <= 10 * 256 * 4
+#pragma unroll 1
+    for (int b = 0; b < NB; ++b) {
+      uint4 v[MAXC];
+      auto addr = [&](int i) { return src + (size_t)b * ld + (tid + i * kCT) * 4; };
+      auto want = [&](int i) { return tid + i * kCT < nq && b < p.B; };
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) v[i] = want(i) ? ldcg_u4(addr(i)) : make_uint4(0, 0, 0, 0);
+      settle(v, addr, want, [&](const uint4 &q) { return tag4_ok(q, tg); });
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = tid + i * kCT;
+        if (c >= nq) continue;
+        const uint4 q = v[i];
+        act[b * aq + c] = b < p.B ? make_uint2((q.x & 0xffffu) | (q.y << 16), (q.z & 0xffffu) | (q.w << 16))
+                                  : make_uint2(0, 0);
+      }
+    }
+  }
 
+#endif
+
+#if !XB_TENSOR_TILES
   // Gated RMSNorm of the DeltaNet core output (HF Qwen3_5RMSNormGated, as called in
   // compiler/qwen35/adapters/delta.py:46-47): y = bf16( bf16(w * bf16(x * r)) * silu(z) ).
   // Each thread derives its head's 1/rms from the eight per-tile partial sums itself.
@@ -782,6 +904,78 @@ template <int NB> struct Consumer {
       }
     }
   }
+#else
+  // Gated RMSNorm of the DeltaNet core output for batch rows 4..8 (same formula as the
+  // small-batch version): the per-tile sums of squares of every (row, head) in one round trip,
+  // reduced by four lanes each ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)); then each row's
+  // core and gate words in one round trip.
+  __device__ void gated_norm_prologue(const bf16 *w, unsigned tg) {
+    uint2 *act = reinterpret_cast<uint2 *>(U);
+    const int HV = p.HV, DK = p.DK, K = HV * DK, nq = K / 4, aq = nq + 2;
+    const int zoff = 2 * p.HK * p.DK + p.HV * p.DK;
+    float *rr = red;          // [NB][HV] 1 / rms
+    constexpr int MAXC = 4;   // K <= 4 * 256 * 4
+    constexpr int MAXS = 4;   // B * HV * 4 <= 4 * 256 (16-byte words of partials)
+    const int nsq = p.B * HV * 4;
+    {
+      uint4 sv[MAXS];
+      auto saddr = [&](int i) { return p.ssq + (size_t)(tid + i * kCT) * 2; };
+      auto swant = [&](int i) { return tid + i * kCT < nsq; };
+#pragma unroll
+      for (int i = 0; i < MAXS; ++i) sv[i] = swant(i) ? ldcg_u4(saddr(i)) : make_uint4(0, 0, 0, 0);
+      settle(sv, saddr, swant, [&](const uint4 &v) { return v.y == tg && v.w == tg; });
+#pragma unroll
+      for (int i = 0; i < MAXS; ++i) {
+        float part = swant(i) ? __uint_as_float(sv[i].x) + __uint_as_float(sv[i].z) : 0.f;
+        part += __shfl_xor_sync(0xffffffffu, part, 1);
+        part += __shfl_xor_sync(0xffffffffu, part, 2);
+        const int k = tid + i * kCT;
+        if ((k & 3) == 0 && k < nsq) rr[k >> 2] = rsqrtf(part / (float)DK + p.eps);
+      }
+    }
+    uint2 wq[MAXC];
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i)
+      wq[i] = tid + i * kCT < nq ? *reinterpret_cast<const uint2 *>(w + ((tid + i * kCT) * 4) % DK)
+                                 : make_uint2(0, 0);
+    csync();
+#pragma unroll 1
+    for (int b = 0; b < NB; ++b) {
+      uint4 xz[2 * MAXC];  // core chunks, then gate (z) chunks
+      auto addr = [&](int k) {
+        const int c = tid + (k % MAXC) * kCT;
+        return k < MAXC ? p.core + (size_t)b * K + c * 4 : p.proj + (size_t)b * p.pstride + zoff + c * 4;
+      };
+      auto want = [&](int k) { return tid + (k % MAXC) * kCT < nq && b < p.B; };
+#pragma unroll
+      for (int k = 0; k < 2 * MAXC; ++k) xz[k] = want(k) ? ldcg_u4(addr(k)) : make_uint4(0, 0, 0, 0);
+      settle(xz, addr, want, [&](const uint4 &v) { return tag4_ok(v, tg); });
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = tid + i * kCT;
+        if (c >= nq) continue;
+        uint2 o = make_uint2(0, 0);
+        if (b < p.B) {
+          const uint4 xv = xz[i], zv = xz[MAXC + i];
+          const uint2 wv = wq[i];
+          const float r = rr[b * HV + (c * 4) / DK];
+          const float x[4] = {bf_lo(xv.x), bf_lo(xv.y), bf_lo(xv.z), bf_lo(xv.w)};
+          const float z[4] = {bf_lo(zv.x), bf_lo(zv.y), bf_lo(zv.z), bf_lo(zv.w)};
+          const float wf[4] = {bf_lo(wv.x), bf_hi(wv.x), bf_lo(wv.y), bf_hi(wv.y)};
+          float y[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float n = rbf(wf[e] * rbf(x[e] * r));
+            y[e] = n * (z[e] / (1.f + expf(-z[e])));
+          }
+          o = make_uint2(pack2(y[0], y[1]), pack2(y[2], y[3]));
+        }
+        act[b * aq + c] = o;
+      }
+    }
+  }
+
+#endif
 
   // Next conv window per channel: [conv[1], conv[2], conv[3], x] for active rows, unchanged for
   // empty rows (recurrent.py:43-52). Runs in the out_proj stage after its prologue has seen
