@@ -132,8 +132,8 @@ int xb_workspace_check(void *workspace, void *stream, int32_t *device_error);
 
 /* Allocation-free decode step. No counterpart in the reference: this entry point exists for
  * callers that cannot allocate device memory when they step the model (a serving runtime that
- * reserved HBM for its own pool at start-up, work issued while a stream is being captured, a
- * host with a fixed memory plan). It takes the geometry and weight pointers directly (no
+ * reserved HBM for its own pool at start-up, a host with a fixed memory plan that forbids
+ * allocations after initialisation). It takes the geometry and weight pointers directly (no
  * XbModel, whose creation allocates) and no workspace: the weight table, RoPE table and the
  * kernel's scratch live in one static device array of XB_STATIC_SCRATCH_BYTES, held by every
  * GPU that loads this library until the process exits. Steps whose scratch would not fit
@@ -143,7 +143,8 @@ int xb_workspace_check(void *workspace, void *stream, int32_t *device_error);
  * All calls on a device share the array, which keeps the previous call's contents: each call
  * rewrites the tables and clears the control words, so calls that overlap on the GPU (other
  * streams, other threads) race and must be serialised by the caller. If device_error is not
- * NULL the call synchronises the stream and reports the kernel's device-side error word. */
+ * NULL the call synchronises the stream and reports the kernel's device-side error word.
+ * Weight pointers follow xb_model_create's rules. */
 #define XB_STATIC_SCRATCH_BYTES (4u << 20)
 int xb_decode_step_static(const XbGeometry *geometry, const XbModelWeights *weights,
                           const XbStepArgs *args, void *stream, int32_t *device_error);

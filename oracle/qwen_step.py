@@ -103,7 +103,10 @@ def apply_rope(x, cos, sin):
 def prefix_attention(q, k_cache, v_cache, length, scale):
     """Decode-row attention over cache[0:length] (attention.cpp:14-79; lower-right causal with
     T == 1 means the whole populated prefix). q [Hq, D], caches [Hkv, C, D]; GQA without expansion.
-    Softmax in fp32; output rounded to bf16."""
+
+    Rounding points of the FlashAttention-2 kernel that attention.cpp:14-79 calls: fp32 scores
+    and exponentials, the row sum taken over the fp32 probabilities, the probabilities rounded to
+    bf16 for the P.V product (fp32 accumulation), the normalised output rounded to bf16."""
     hq, d = q.shape
     hkv = k_cache.shape[0]
     group = hq // hkv
@@ -111,8 +114,10 @@ def prefix_attention(q, k_cache, v_cache, length, scale):
     v = v_cache[:, :length].float()
     qg = q.view(hkv, group, d)
     scores = torch.einsum("hgd,hld->hgl", qg, k) * scale
-    p = torch.softmax(scores, dim=-1)
-    return rbf(torch.einsum("hgl,hld->hgd", p, v).reshape(hq, d))
+    p = torch.exp(scores - scores.amax(-1, keepdim=True))
+    lsum = p.sum(-1, keepdim=True)
+    o = torch.einsum("hgl,hld->hgd", rbf(p), v) / lsum
+    return rbf(o.reshape(hq, d))
 
 
 def deltanet_core(qkv, b, a, conv, state, conv_w, a_log, dt_bias, active, hk, hv, dk):

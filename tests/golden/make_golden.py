@@ -47,7 +47,7 @@ sys.path.insert(0, str(REPO))
 from xinfer_b200 import configs, synthetic  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
-SAMPLES = 2048
+SAMPLES = 4096
 
 
 @triton.jit
@@ -284,11 +284,14 @@ def make_schedules(geometry, kind, seed):
         return [[[tok()] if a else [] for a in row] for row in active]
     if kind == "short":
         return [[[tok()]] for _ in range(4)]
+    if kind == "long16":
+        return [[[tok()]] for _ in range(16)]
     raise ValueError(kind)
 
 
 CASES = {
-    # name: (config, schedule kind, capacity, jitter, full logits)
+    # name: (config, schedule kind, capacity, jitter, full logits: True, False, or the number of
+    # final steps whose full rows are stored)
     "qwen3-tiny-single": ("qwen3-tiny", "single", 16, 0.1, True),
     "qwen3-tiny-batch": ("qwen3-tiny", "batch", 16, 0.1, True),
     "qwen3.5-tiny-single": ("qwen3.5-tiny", "single", 16, 0.1, True),
@@ -296,6 +299,9 @@ CASES = {
     "qwen3.5-tiny-hv32-single": ("qwen3.5-tiny-hv32", "single", 16, 0.1, True),
     "qwen3-0.6b-short": ("qwen3-0.6b", "short", 16, 0.0, False),
     "qwen3.5-0.8b-short": ("qwen3.5-0.8b", "short", 16, 0.0, False),
+    # the headline geometry at the headline KV capacity: full depth, 4096 slots, 16 steps, the
+    # last 8 logits rows stored whole (one reference step takes about a minute on the CPU)
+    "qwen3.5-0.8b-cap4096": ("qwen3.5-0.8b", "long16", 4096, 0.0, 8),
 }
 
 
@@ -318,11 +324,12 @@ def generate(ref, name, seed=0):
     fixture = {
         "name": name, "config": config, "seed": seed, "jitter": jitter, "capacity": capacity,
         "schedule": schedule, "positions": positions,
-        "logits": logits if full else None,
+        "logits": logits if full is True else None,
+        "logits_tail": logits[-full:].clone() if full is not True and full else None,
         "logits_summary": summarize_logits(logits),
         "state_sample": sample_state(state),
         "conv_state": [t.clone() for i, t in enumerate(state)
-                       if geometry.is_delta(i // 2) and i % 2 == 0] if full else None,
+                       if geometry.is_delta(i // 2) and i % 2 == 0] if full is True else None,
     }
     out = HERE / f"{name}.pt"
     torch.save(fixture, out)

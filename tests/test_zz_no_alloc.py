@@ -1,8 +1,7 @@
 """The allocation-free decode entry point (xb_decode_step_static) against the regular one.
 
 xb_decode_step_static serves callers that cannot allocate device memory while they step the
-model (a runtime that has reserved HBM for its own pool, work issued during stream capture, a
-fixed memory plan): it keeps its scratch in a static device array instead of a caller
+model (a runtime that has reserved HBM for its own pool at start-up, a fixed memory plan): it keeps its scratch in a static device array instead of a caller
 workspace. This test drives both entry points through the C ABI on identical inputs for two
 calls in a row and compares logits and greedy tokens with the tolerance of the other parity
 tests. It sits in its own file, collected last, and builds everything it needs itself.

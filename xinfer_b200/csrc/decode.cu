@@ -59,7 +59,7 @@ static WsLayout ws_layout(const XbGeometry &g, int max_batch, int ncta) {
   L.core = take((size_t)B * vdim * 4);
   L.ssq = take((size_t)B * (q35 ? g.lin_value_heads : 1) * 8 * 8);
   L.att_o = take((size_t)B * g.num_q_heads * L.max_splits * g.head_dim * 8);
-  L.att_ml = take((size_t)B * g.num_q_heads * L.max_splits * 16);
+  L.att_ml = take((size_t)B * g.num_q_heads * L.max_splits * 16);  // (M, L) pairs
   L.att_out = take((size_t)B * g.num_q_heads * g.head_dim * 4);
   L.act = take((size_t)B * g.intermediate * 4);
   L.am_v = take((size_t)ncta * XB_MAX_BATCH * 4);
@@ -107,6 +107,48 @@ static int check_geometry(const XbGeometry &g) {
   if (kmax * 2 > kSlot || g.hidden * 4 > kSlot)
     return fail(XB_ERR_UNSUPPORTED, "GEMV input dimension too large for a ring slot");
   return XB_OK;
+}
+
+// Weight pointers: every tensor the geometry uses must be present, and the matrices the kernel
+// streams with bulk copies (and lm_head) must be 16-byte aligned. Shared by xb_model_create and
+// xb_decode_step_static.
+static int check_weights(const XbGeometry &g, const XbModelWeights &weights) {
+  auto aligned = [](const void *ptr) { return ((uintptr_t)ptr & 15) == 0; };
+  if (!weights.embed || !weights.final_norm || !weights.lm_head)
+    return fail(XB_ERR_INVALID, "embed, final_norm and lm_head are required");
+  if (!aligned(weights.lm_head)) return fail(XB_ERR_INVALID, "lm_head must be 16-byte aligned");
+  for (int l = 0; l < g.num_layers; ++l) {
+    const XbLayerWeights &w = weights.layers[l];
+    std::vector<const void *> need = {w.input_norm, w.post_norm, w.gate, w.up, w.down};
+    std::vector<const void *> streamed = {w.gate, w.up, w.down};
+    if (g.layer_kind[l] == XB_LAYER_DELTANET) {
+      for (auto q : {w.in_qkv, w.in_z, w.in_b, w.in_a, w.conv_w, w.a_log, w.dt_bias, w.gnorm,
+                     w.out_proj})
+        need.push_back(q);
+      for (auto q : {w.in_qkv, w.in_z, w.in_b, w.in_a, w.out_proj}) streamed.push_back(q);
+    } else {
+      for (auto q : {w.q_proj, w.k_proj, w.v_proj, w.o_proj, w.q_norm, w.k_norm}) need.push_back(q);
+      for (auto q : {w.q_proj, w.k_proj, w.v_proj, w.o_proj}) streamed.push_back(q);
+    }
+    for (auto q : need)
+      if (!q) return fail(XB_ERR_INVALID, "missing weight pointer in layer " + std::to_string(l));
+    for (auto q : streamed)
+      if (!aligned(q))
+        return fail(XB_ERR_INVALID, "projection weights must be 16-byte aligned (layer " +
+                                        std::to_string(l) + ")");
+  }
+  return XB_OK;
+}
+
+// The workspace layout is fixed by the workspace size: the largest batch whose layout fits, so
+// the tagged words keep their addresses whatever batch size and split count a launch uses.
+static int ws_layout_for(const XbGeometry &g, size_t workspace_bytes, int ncta, WsLayout &L, int &bcap) {
+  for (int b = XB_MAX_BATCH; b >= 1; --b) {
+    L = ws_layout(g, b, ncta);
+    if (L.total <= workspace_bytes) { bcap = b; return XB_OK; }
+  }
+  bcap = 0;
+  return fail(XB_ERR_INVALID, "workspace too small");
 }
 
 static size_t ubytes_for(const XbGeometry &g, int NB) {
@@ -171,30 +213,8 @@ int xb_model_create(const XbGeometry *geometry, const XbModelWeights *weights, X
   int rc = check_geometry(*geometry);
   if (rc) return rc;
   const XbGeometry &g = *geometry;
-  auto aligned = [](const void *ptr) { return ((uintptr_t)ptr & 15) == 0; };
-  if (!weights->embed || !weights->final_norm || !weights->lm_head)
-    return fail(XB_ERR_INVALID, "embed, final_norm and lm_head are required");
-  if (!aligned(weights->lm_head)) return fail(XB_ERR_INVALID, "lm_head must be 16-byte aligned");
-  for (int l = 0; l < g.num_layers; ++l) {
-    const XbLayerWeights &w = weights->layers[l];
-    std::vector<const void *> need = {w.input_norm, w.post_norm, w.gate, w.up, w.down};
-    std::vector<const void *> streamed = {w.gate, w.up, w.down};
-    if (g.layer_kind[l] == XB_LAYER_DELTANET) {
-      for (auto q : {w.in_qkv, w.in_z, w.in_b, w.in_a, w.conv_w, w.a_log, w.dt_bias, w.gnorm,
-                     w.out_proj})
-        need.push_back(q);
-      for (auto q : {w.in_qkv, w.in_z, w.in_b, w.in_a, w.out_proj}) streamed.push_back(q);
-    } else {
-      for (auto q : {w.q_proj, w.k_proj, w.v_proj, w.o_proj, w.q_norm, w.k_norm}) need.push_back(q);
-      for (auto q : {w.q_proj, w.k_proj, w.v_proj, w.o_proj}) streamed.push_back(q);
-    }
-    for (auto q : need)
-      if (!q) return fail(XB_ERR_INVALID, "missing weight pointer in layer " + std::to_string(l));
-    for (auto q : streamed)
-      if (!aligned(q))
-        return fail(XB_ERR_INVALID, "projection weights must be 16-byte aligned (layer " +
-                                        std::to_string(l) + ")");
-  }
+  rc = check_weights(g, *weights);
+  if (rc) return rc;
   XbModel *m = new XbModel();
   m->g = g;
   m->w = *weights;
@@ -285,8 +305,12 @@ int xb_decode_step(const XbModel *model, const XbStepArgs *args, void *workspace
     }
   }
   const int ncta = model->num_sms;
-  const WsLayout Lb = ws_layout(g, B, ncta);
-  if (workspace_bytes < Lb.total) return fail(XB_ERR_INVALID, "workspace too small");
+  WsLayout Lb;
+  int bcap = 0;
+  int lrc = ws_layout_for(g, workspace_bytes, ncta, Lb, bcap);
+  if (lrc) return lrc;
+  if (bcap < B)
+    return fail(XB_ERR_INVALID, "workspace too small for batch " + std::to_string(B));
   if (((uintptr_t)workspace & 255) != 0) return fail(XB_ERR_INVALID, "workspace must be 256-byte aligned");
 
   StepParams p;
@@ -344,13 +368,16 @@ int xb_decode_step(const XbModel *model, const XbStepArgs *args, void *workspace
   p.h = (unsigned *)(ws + Lb.h);
   p.proj = (unsigned *)(ws + Lb.proj);
   p.core = (unsigned *)(ws + Lb.core);
-  p.ssq = (uint2 *)(ws + Lb.ssq);
-  p.att_o = (uint2 *)(ws + Lb.att_o);
-  p.att_ml = (uint4 *)(ws + Lb.att_ml);
+  p.ssq = (u64 *)(ws + Lb.ssq);
+  p.att_o = (u64 *)(ws + Lb.att_o);
+  p.att_ml = (u64 *)(ws + Lb.att_ml);
   p.att_out = (unsigned *)(ws + Lb.att_out);
   p.act = (unsigned *)(ws + Lb.act);
   p.am_v = (float *)(ws + Lb.am_v);
   p.am_i = (int *)(ws + Lb.am_i);
+  // everything after the control words, up to the end of the workspace
+  p.scrub_base = (uint4 *)(ws + Lb.h);
+  p.scrub_chunks = (unsigned)((workspace_bytes - Lb.h) / 16);
   p.trace = g_trace;
 
   const int NB = B <= 1 ? 1 : B <= 2 ? 2 : B <= 4 ? 4 : 8;
@@ -377,9 +404,8 @@ int xb_decode_step(const XbModel *model, const XbStepArgs *args, void *workspace
 //
 // Some callers cannot allocate device memory at the moment they run a decode step: serving
 // stacks that reserve (nearly) all of HBM for their own pool at start-up, so a later cudaMalloc
-// fails or fragments that pool; code that runs while a stream is being captured, where a
-// cudaMalloc would not be part of the captured work; and hosts with a fixed memory plan that
-// forbids allocations after initialisation. This entry point needs neither an XbModel (whose
+// fails or fragments that pool, and hosts with a fixed memory plan that forbids allocations
+// after initialisation. This entry point needs neither an XbModel (whose
 // creation allocates the weight table) nor a caller workspace: the per-layer weight table, the
 // RoPE table and the kernel's scratch all live in one file-scope device array of
 // XB_STATIC_SCRATCH_BYTES, which every GPU that loads this library keeps until the process exits.
@@ -447,25 +473,9 @@ extern "C" int xb_decode_step_static(const XbGeometry *geometry, const XbModelWe
   unsigned char *table = sd.base;
   unsigned char *rope = sd.base + kStaticTableBytes;
   unsigned char *ws = sd.base + kStaticWsOffset;
-  // Same weight-pointer rules as xb_model_create: present, and 16-byte aligned where the kernel
-  // streams them with bulk copies.
-  if (!weights->embed || !weights->final_norm || !weights->lm_head || ((uintptr_t)weights->lm_head & 15))
-    return fail(XB_ERR_INVALID, "embed, final_norm and a 16-byte aligned lm_head are required");
-  for (int l = 0; l < g.num_layers; ++l) {
-    const XbLayerWeights &w = weights->layers[l];
-    const bool delta = g.layer_kind[l] == XB_LAYER_DELTANET;
-    const void *need[] = {w.input_norm, w.post_norm, w.gate, w.up, w.down,
-                          delta ? w.in_qkv : w.q_proj, delta ? w.in_z : w.k_proj,
-                          delta ? w.in_b : w.v_proj, delta ? w.out_proj : w.o_proj,
-                          delta ? w.in_a : w.q_norm, delta ? w.conv_w : w.k_norm,
-                          delta ? w.a_log : w.input_norm, delta ? w.dt_bias : w.input_norm,
-                          delta ? w.gnorm : w.input_norm};
-    for (int i = 0; i < 14; ++i) {
-      if (!need[i]) return fail(XB_ERR_INVALID, "missing weight pointer in layer " + std::to_string(l));
-      if (i < 10 && ((uintptr_t)need[i] & 15))
-        return fail(XB_ERR_INVALID, "projection weights must be 16-byte aligned");
-    }
-  }
+  // The same weight-pointer rules as xb_model_create.
+  rc = check_weights(g, *weights);
+  if (rc) return rc;
   // Stage the weight table and RoPE frequencies into the static array (stream-ordered copies
   // from host memory; no allocation). Every call rewrites them.
   float inv[kStaticRopeBytes / sizeof(float)];
@@ -484,8 +494,9 @@ extern "C" int xb_decode_step_static(const XbGeometry *geometry, const XbModelWe
   m.d_inv_freq = reinterpret_cast<float *>(rope);
   m.device = dev;
   m.num_sms = sd.num_sms;
-  // Same validation and launch as xb_decode_step; the model is a host-stack view (the weight
-  // pointers of `weights` must also satisfy xb_model_create's alignment rules).
+  // Same validation and launch as xb_decode_step; the model is a host-stack view. The scratch
+  // is the whole rest of the array, so the kernel's periodic clear of its tagged words covers
+  // what any earlier call (of any model) wrote there.
   rc = xb_decode_step(&m, args, ws, ws_room, stream);
   if (rc) return rc;
   if (device_error) {

@@ -62,8 +62,12 @@ constexpr int RED_PART = 512;   // [2][kWarps][2][NB][2] split-K partials (batch
 
 // control words in the workspace (each on its own 128-byte line)
 // Words [0, CTL_WORDS) are cleared whenever a workspace is reset; the launch epoch (which
-// stamps every inter-stage value with a tag) lives after them and only ever advances.
-enum { CTL_ERR = 64, CTL_DONE = 96, CTL_WORDS = 128, CTL_EPOCH = 128, CTL_TOTAL = 160 };
+// stamps every inter-stage value with a tag) and the epoch of the last clear of the tagged
+// buffers live after them.
+enum {
+  CTL_SCRUB_BAR = 32, CTL_ERR = 64, CTL_DONE = 96, CTL_WORDS = 128, CTL_EPOCH = 128,
+  CTL_SCRUBBED = 160, CTL_TOTAL = 192
+};
 // device error codes
 enum { DERR_WAIT = 1, DERR_RING_FULL = 2, DERR_RING_EMPTY = 3, DERR_TOKEN = 4, DERR_DRAIN = 5 };
 
@@ -94,8 +98,11 @@ struct StepParams {
   unsigned *ctrl;
   // inter-stage buffers of tagged words: (bf16 bits | tag << 16) or {fp32 bits, tag}
   unsigned *h, *proj, *core, *att_out, *act;
-  uint2 *ssq, *att_o;
-  uint4 *att_ml;
+  u64 *ssq, *att_o, *att_ml;  // {fp32, tag} words; att_ml holds (M, L) pairs
+  // the tagged buffers as one range [scrub_base, scrub_base + 16 * scrub_chunks), cleared by
+  // the launches that start kScrubInterval or more epochs after the previous clear
+  uint4 *scrub_base;
+  unsigned scrub_chunks;
   float *am_v;
   int *am_i;
   // Optional stage trace (see xb_debug_trace): per CTA kTraceStages x {arrive, release} stamps
@@ -112,6 +119,7 @@ struct SmemHdr {
   long long pos[XB_MAX_BATCH];
   int abort;
   int is_last;
+  int scrub;  // this launch clears the tagged buffers before any stage runs
   unsigned epoch;
 };
 static_assert(sizeof(SmemHdr) <= kHdrBytes, "header");
@@ -423,27 +431,27 @@ static __device__ __noinline__ unsigned repoll1(const unsigned *w, unsigned tg, 
   }
   return v;
 }
-static __device__ __noinline__ uint4 repoll2f(const uint2 *w, unsigned tg, volatile int *abort_flag,
-                                       unsigned *ctrl) {
-  uint4 v;
+static __device__ __noinline__ ulonglong2 repoll2f(const u64 *w, unsigned tg, volatile int *abort_flag,
+                                             unsigned *ctrl) {
+  ulonglong2 v;
   uint64_t t0 = 0;
   for (unsigned spins = 1;; ++spins) {
-    v = ld_poll_u4(w);
-    if (v.y == tg && v.w == tg) break;
+    v = ld_poll_u64x2(w);
+    if (ftag_tag(v.x) == tg && ftag_tag(v.y) == tg) break;
     if ((spins & 15u) == 0 && wait_give_up(abort_flag, ctrl, t0)) break;
   }
   return v;
 }
-static __device__ __noinline__ float repoll1f(const uint2 *w, unsigned tg, volatile int *abort_flag,
+static __device__ __noinline__ float repoll1f(const u64 *w, unsigned tg, volatile int *abort_flag,
                                        unsigned *ctrl) {
-  uint2 v;
+  u64 v;
   uint64_t t0 = 0;
   for (unsigned spins = 1;; ++spins) {
-    v = ld_poll_u2(w);
-    if (v.y == tg) break;
+    v = ld_poll_u64(w);
+    if (ftag_tag(v) == tg) break;
     if ((spins & 15u) == 0 && wait_give_up(abort_flag, ctrl, t0)) break;
   }
-  return __uint_as_float(v.x);
+  return ftag_val(v);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -532,9 +540,9 @@ template <int NB> struct Consumer {
     const unsigned v = ld_poll_u32(w);
     return (v >> 16) == tg ? v : repoll1(w, tg, abort_flag(), p.ctrl);
   }
-  __device__ __forceinline__ uint4 poll2f(const uint2 *w, unsigned tg) const {
-    const uint4 v = ldcg_u4(w);
-    return (v.y == tg && v.w == tg) ? v : repoll2f(w, tg, abort_flag(), p.ctrl);
+  __device__ __forceinline__ ulonglong2 poll2f(const u64 *w, unsigned tg) const {
+    const ulonglong2 v = ldcg_u64x2(w);
+    return (ftag_tag(v.x) == tg && ftag_tag(v.y) == tg) ? v : repoll2f(w, tg, abort_flag(), p.ctrl);
   }
 
   // Completes a batch of tagged loads: words v[i] with want(i) that are not ok() yet are loaded
@@ -569,6 +577,25 @@ template <int NB> struct Consumer {
       late = false;
 #pragma unroll
       for (int i = 0; i < N; ++i) late |= want(i) && (v[i] >> 16) != tg;
+      if (late && (round & 15u) == 0 && give_up(t0)) break;
+    }
+  }
+
+  // settle() for vectors of two {fp32, tag} words.
+  template <int N, class Addr, class Want>
+  __device__ __forceinline__ void settle64(ulonglong2 (&v)[N], Addr addr, Want want, unsigned tg) const {
+    auto ok = [&](const ulonglong2 &w) { return ftag_tag(w.x) == tg && ftag_tag(w.y) == tg; };
+    bool late = false;
+#pragma unroll
+    for (int i = 0; i < N; ++i) late |= want(i) && !ok(v[i]);
+    uint64_t t0 = 0;
+    for (unsigned round = 1; late; ++round) {
+#pragma unroll
+      for (int i = 0; i < N; ++i)
+        if (want(i) && !ok(v[i])) v[i] = ld_poll_u64x2(addr(i));
+      late = false;
+#pragma unroll
+      for (int i = 0; i < N; ++i) late |= want(i) && !ok(v[i]);
       if (late && (round & 15u) == 0 && give_up(t0)) break;
     }
   }
@@ -880,13 +907,13 @@ template <int NB> struct Consumer {
           const uint4 zv = poll4(p.proj + (size_t)b * p.pstride + zoff + c * 4, tg);
           const uint2 wv = *reinterpret_cast<const uint2 *>(w + (c * 4) % DK);
           const int h = (c * 4) / DK;
-          const uint2 *ps = p.ssq + ((size_t)b * p.HV + h) * 8;
+          const u64 *ps = p.ssq + ((size_t)b * p.HV + h) * 8;
           float tot = 0.f;
 #pragma unroll
           for (int t = 0; t < 8; t += 2) {
-            const uint4 q = poll2f(ps + t, tg);
-            tot += __uint_as_float(q.x);
-            tot += __uint_as_float(q.z);
+            const ulonglong2 q = poll2f(ps + t, tg);
+            tot += ftag_val(q.x);
+            tot += ftag_val(q.y);
           }
           const float r = rsqrtf(tot / (float)DK + p.eps);
           const float x[4] = {bf_lo(xv.x), bf_lo(xv.y), bf_lo(xv.z), bf_lo(xv.w)};
@@ -918,15 +945,15 @@ template <int NB> struct Consumer {
     constexpr int MAXS = 4;   // B * HV * 4 <= 4 * 256 (16-byte words of partials)
     const int nsq = p.B * HV * 4;
     {
-      uint4 sv[MAXS];
+      ulonglong2 sv[MAXS];
       auto saddr = [&](int i) { return p.ssq + (size_t)(tid + i * kCT) * 2; };
       auto swant = [&](int i) { return tid + i * kCT < nsq; };
 #pragma unroll
-      for (int i = 0; i < MAXS; ++i) sv[i] = swant(i) ? ldcg_u4(saddr(i)) : make_uint4(0, 0, 0, 0);
-      settle(sv, saddr, swant, [&](const uint4 &v) { return v.y == tg && v.w == tg; });
+      for (int i = 0; i < MAXS; ++i) sv[i] = swant(i) ? ldcg_u64x2(saddr(i)) : make_ulonglong2(0, 0);
+      settle64(sv, saddr, swant, tg);
 #pragma unroll
       for (int i = 0; i < MAXS; ++i) {
-        float part = swant(i) ? __uint_as_float(sv[i].x) + __uint_as_float(sv[i].z) : 0.f;
+        float part = swant(i) ? ftag_val(sv[i].x) + ftag_val(sv[i].y) : 0.f;
         part += __shfl_xor_sync(0xffffffffu, part, 1);
         part += __shfl_xor_sync(0xffffffffu, part, 2);
         const int k = tid + i * kCT;
@@ -1348,6 +1375,10 @@ template <int NB> struct Consumer {
       if (tid == 0) {
         // every CTA has consumed all tagged inputs of this launch before taking a ticket
         p.ctrl[CTL_EPOCH] = epoch + 1u;  // also after an abort: stale tags never match again
+        if (hdr->scrub) {
+          p.ctrl[CTL_SCRUBBED] = epoch;
+          p.ctrl[CTL_SCRUB_BAR] = 0u;
+        }
         atomicExch(p.ctrl + CTL_DONE, 0u);
       }
     }
@@ -1389,13 +1420,13 @@ template <int NB> struct Consumer {
 #pragma unroll
       for (int i = 0; i < 8; ++i) S[i] = S_in[(size_t)(rbase + i) * DK + col];
       unsigned *core = p.core + (size_t)b * HV * DK + h * DK + t * 16;
-      uint2 *ssq = p.ssq + ((size_t)b * HV + h) * 8 + t;
+      u64 *ssq = p.ssq + ((size_t)b * HV + h) * 8 + t;
       if (p.q_len[b] == 0) {
         // Empty row: replacement state equals the input state (a no-op when in place).
 #pragma unroll
         for (int i = 0; i < 8; ++i) S_out[(size_t)(rbase + i) * DK + col] = S[i];
         if (tid < 16) core[tid] = tagged(0.f, tg);
-        if (tid == 0) *ssq = make_uint2(0u, tg);
+        if (tid == 0) st_u64(ssq, ftag(0.f, tg));
         continue;
       }
       const bf16 *cin = conv_in_all + (size_t)b * CH * CW;
@@ -1493,7 +1524,7 @@ template <int NB> struct Consumer {
         float sq = ob * ob;
 #pragma unroll
         for (int o2 = 8; o2; o2 >>= 1) sq += __shfl_xor_sync(0x0000ffffu, sq, o2);
-        if (tid == 0) *ssq = make_uint2(__float_as_uint(sq), tg);
+        if (tid == 0) st_u64(ssq, ftag(sq, tg));
       }
     }
   }
@@ -1648,9 +1679,11 @@ template <int NB> struct Consumer {
         const float corr = expf(m - mn);
         const float pe = expf(sc - mn);
         lsum = lsum * corr + pe;
+        // FlashAttention-2 rounding: the row sum over fp32 probabilities, P.V over bf16 ones
+        const float pb = rbf(pe);
 #pragma unroll
         for (int e = 0; e < 8; ++e)
-          if (e < EPL) o[e] = fmaf(pe, vf[e], o[e] * corr);
+          if (e < EPL) o[e] = fmaf(pb, vf[e], o[e] * corr);
         m = mn;
       }
       // merge the P partial states of each head
@@ -1678,8 +1711,8 @@ template <int NB> struct Consumer {
         }
         const int hq = kvh * G + gg;
         const size_t base = ((size_t)b * HQ + hq) * splits + s;
-        p.att_o[base * D + d] = make_uint2(__float_as_uint(O), tg);
-        if (d == 0) p.att_ml[base] = make_uint4(__float_as_uint(M), tg, __float_as_uint(Lw), tg);
+        st_u64(p.att_o + base * D + d, ftag(O, tg));
+        if (d == 0) st_u64x2(p.att_ml + 2 * base, ftag(M, tg), ftag(Lw, tg));
       }
       csync();
     }
@@ -1709,17 +1742,11 @@ template <int NB> struct Consumer {
       }
       const size_t base = ((size_t)b * HQ + hq) * splits;
       for (int s = tid; s < splits; s += kCT) {
-        uint4 v = ldcg_u4(p.att_ml + base + s);
-        if (v.y != tg || v.w != tg) {
-          uint64_t t0 = 0;
-          for (unsigned spins = 1;; ++spins) {
-            v = ld_poll_u4(p.att_ml + base + s);
-            if (v.y == tg && v.w == tg) break;
-            if ((spins & 15u) == 0 && give_up(t0)) break;
-          }
-        }
-        ms[s] = __uint_as_float(v.x);
-        ls[s] = __uint_as_float(v.z);
+        ulonglong2 v = ldcg_u64x2(p.att_ml + 2 * (base + s));
+        if (ftag_tag(v.x) != tg || ftag_tag(v.y) != tg)
+          v = repoll2f(p.att_ml + 2 * (base + s), tg, abort_flag(), p.ctrl);
+        ms[s] = ftag_val(v.x);
+        ls[s] = ftag_val(v.y);
       }
       csync();
       float M = -INFINITY;
@@ -1728,20 +1755,20 @@ template <int NB> struct Consumer {
       if (M != -INFINITY) {
         constexpr int MSP = 10;  // splits handled per pass per warp
         for (int s0 = warp; s0 < splits; s0 += kWarps * MSP) {
-          uint2 vo[MSP];
+          u64 vo[MSP];
 #pragma unroll
           for (int i = 0; i < MSP; ++i) {
             const int s = s0 + i * kWarps;
-            vo[i] = (s < splits && ms[s] != -INFINITY) ? __ldcg(p.att_o + (base + s) * D + d)
-                                                       : make_uint2(0u, tg);
+            vo[i] = (s < splits && ms[s] != -INFINITY) ? ldcg_u64(p.att_o + (base + s) * D + d)
+                                                       : ftag(0.f, tg);
           }
 #pragma unroll
           for (int i = 0; i < MSP; ++i) {
             const int s = s0 + i * kWarps;
             if (s >= splits || ms[s] == -INFINITY) continue;
-            const float ov = vo[i].y == tg ? __uint_as_float(vo[i].x)
-                                           : repoll1f(p.att_o + (base + s) * D + d, tg, abort_flag(),
-                                                      p.ctrl);
+            const float ov = ftag_tag(vo[i]) == tg ? ftag_val(vo[i])
+                                                   : repoll1f(p.att_o + (base + s) * D + d, tg, abort_flag(),
+                                                              p.ctrl);
             const float f = expf(ms[s] - M);
             O = fmaf(ov, f, O);
             Lw = fmaf(ls[s], f, Lw);
@@ -1786,6 +1813,31 @@ template <class V> __device__ __forceinline__ void walk_step(const StepParams &p
   v.gemv(-1, ST_LMHEAD);
 }
 
+// Clears this CTA's share of the tagged buffers, then waits (bounded) until every CTA has cleared
+// its share, so that no stage of this launch writes a value that another CTA's clear erases.
+// Every thread of the CTA takes part. The last CTA of the launch records the epoch of the clear
+// and resets the arrival counter.
+static __device__ __noinline__ void scrub_tagged(const StepParams &p) {
+  int lo, hi;
+  cta_range((int)p.scrub_chunks, blockIdx.x, p.ncta, lo, hi);
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  for (int i = lo + (int)threadIdx.x; i < hi; i += kThreads) __stcg(p.scrub_base + i, z);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(p.ctrl + CTL_SCRUB_BAR, 1u);
+    const uint64_t t0 = globaltimer();
+    while (ld_acquire(p.ctrl + CTL_SCRUB_BAR) < (unsigned)p.ncta) {
+      if (ld_volatile(p.ctrl + CTL_ERR)) break;
+      if (globaltimer() - t0 > c_wait_limit_ns) {
+        atomicCAS(p.ctrl + CTL_ERR, 0u, (unsigned)DERR_WAIT);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+}
+
 template <int NB>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ StepParams p) {
   extern __shared__ __align__(1024) char smem[];
@@ -1803,6 +1855,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     hdr->abort = 0;
     hdr->is_last = 0;
     hdr->epoch = ld_volatile(p.ctrl + CTL_EPOCH);
+    // unsigned difference: an epoch moved backwards also counts as "long ago"
+    hdr->scrub = hdr->epoch - ld_volatile(p.ctrl + CTL_SCRUBBED) >= kScrubInterval;
     mbar_fence_init();
   }
   // validate token ids once (out-of-range ids are recorded and read as id 0 nowhere: abort)
@@ -1814,6 +1868,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     if (id < 0 || id >= p.V) atomicCAS(p.ctrl + CTL_ERR, 0u, (unsigned)DERR_TOKEN);
   }
   __syncthreads();
+  if (hdr->scrub) scrub_tagged(p);
   const bool bad = ld_volatile(p.ctrl + CTL_ERR) != 0;
   if (threadIdx.x >= kCT) {
     if (threadIdx.x == kCT && !bad) {

@@ -116,10 +116,49 @@ __device__ __forceinline__ uint2 ldg_u2(const void *p) {
 // ---- tagged inter-stage words --------------------------------------------------------------
 // A bf16 value travels with a 16-bit tag in one 32-bit word, (tag << 16) | bits, so a consumer
 // that sees the expected tag also sees the value: no fence or flag is needed between stages.
-// Tags are derived from the launch epoch and the (layer, write) position and are never 0, so a
-// zeroed or stale buffer never looks ready.
+// tag = (epoch mod 511) * 128 + (2 * layer + k) + 1 (layer < 64, k in {0, 1}): never 0, so a
+// zeroed word never looks ready; distinct for every (layer, k) of one launch; and equal for two
+// launches only when their epochs differ by a multiple of kTagPeriod. The kernel clears every
+// tagged buffer at least once per kScrubInterval (< kTagPeriod) launches, so no word a launch
+// polls can carry a stale tag equal to the one it waits for.
+constexpr unsigned kTagPeriod = 511;
+constexpr unsigned kScrubInterval = 256;
 __device__ __forceinline__ unsigned tag_of(unsigned epoch, int layer, int k) {
-  return (unsigned)(((unsigned long long)epoch * 160ull + (unsigned)(layer * 2 + k)) % 65535ull) + 1u;
+  return (epoch % kTagPeriod) * 128u + (unsigned)(layer * 2 + k) + 1u;
+}
+// {fp32 value, tag} pairs travel as one 64-bit word (value in the low half), stored and loaded
+// as 64-bit scalars (or as vectors of them), each single-copy atomic.
+typedef unsigned long long u64;
+__device__ __forceinline__ u64 ftag(float v, unsigned tag) {
+  return ((u64)tag << 32) | (u64)__float_as_uint(v);
+}
+__device__ __forceinline__ float ftag_val(u64 w) { return __uint_as_float((unsigned)w); }
+__device__ __forceinline__ unsigned ftag_tag(u64 w) { return (unsigned)(w >> 32); }
+__device__ __forceinline__ void st_u64(u64 *p, u64 v) {
+  asm volatile("st.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_u64x2(u64 *p, u64 a, u64 b) {
+  asm volatile("st.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ u64 ldcg_u64(const u64 *p) {
+  u64 v;
+  asm volatile("ld.global.cg.u64 %0, [%1];" : "=l"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ ulonglong2 ldcg_u64x2(const u64 *p) {
+  ulonglong2 v;
+  asm volatile("ld.global.cg.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ u64 ld_poll_u64(const u64 *p) {
+  u64 v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ ulonglong2 ld_poll_u64x2(const u64 *p) {
+  ulonglong2 v;
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+  return v;
 }
 __device__ __forceinline__ unsigned tagged(float v, unsigned tag) {
   return (tag << 16) | (unsigned)__bfloat16_as_ushort(__float2bfloat16_rn(v));
