@@ -11,7 +11,12 @@ random-init bf16 weights, batch 1, a 512-token uniform-random prompt, then greed
          host->device copy of token id + position and a device->host read of the next token,
          then a host sync (wall clock over the K steps)
   roofline  algorithmic bytes per token / mean launch time vs the measured HBM copy peak
-  cpu_baseline  the CPU oracle (a port of the reference step) on this host's cores, bounded
+  cpu_baseline  the unchanged HF transformers model, eager, bf16, on this host's cores, with the
+         call pattern of the reference's HF benchmark worker (tools/benchmark/common.py:237-267):
+         the whole prompt in one call (untimed), then one forced token per call with
+         logits_to_keep=1, argmax and host read per step; all host threads, and the 1-thread
+         figure (the reference's thread policy) beside it. The fp32 CPU oracle's decode rate is
+         reported as a secondary figure.
 Multi-GPU (torchrun, one process per GPU): independent replicas, no collective on the data
 path; the timed region is bracketed by barriers and the slowest rank's time is reported.
 
@@ -48,7 +53,8 @@ def parse():
                     help="prompt length (batch > 1: the largest of the rows' random lengths)")
     ap.add_argument("--batch", type=int, default=1, help="rows per GPU, 1..8, ragged prompts")
     ap.add_argument("--capacity", type=int, default=4096)
-    ap.add_argument("--cpu-seconds", type=float, default=20.0, help="budget of the CPU baseline")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="budget of the secondary CPU-oracle figure")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--trace", help="save a per-CTA stage trace of one extra step to this file")
     return ap.parse_args()
@@ -187,9 +193,84 @@ class Clocks:
                 "samples": len(mhz)}
 
 
-def cpu_baseline(args, g, budget_s):
+def hf_eager_model(g):
+    """The unchanged HF text model, built as the reference's loaders build it
+    (compiler/qwen35/model.py:21-42, compiler/qwen3/model.py:16-26): sdpa attention, bf16, tied
+    lm_head, RoPE buffers recreated in fp32; the seeded synthetic weights of the GPU run instead
+    of a checkpoint; on the CPU."""
+    from xinfer_b200 import configs, synthetic
+
+    hf = configs.hf_config(g)
+    hf._attn_implementation = "sdpa"
+    if g.family == configs.QWEN35:
+        from transformers import Qwen3_5ForCausalLM as Model
+        from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5TextRotaryEmbedding as Rotary
+    else:
+        from transformers import Qwen3ForCausalLM as Model
+        from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding as Rotary
+    with torch.device("meta"):
+        model = Model(hf)
+    model.load_state_dict(synthetic.make_state_dict(g, seed=0), strict=True, assign=True)
+    model.lm_head.weight = model.model.embed_tokens.weight
+    model.model.rotary_emb = Rotary(hf)
+    return model.eval().requires_grad_(False)
+
+
+def hf_eager_baseline(g, prompt_len, steps, warmup, threads_list):
+    """Decode tokens/s of the HF eager model on the CPU, one figure per thread count.
+
+    The reference's HF worker (tools/benchmark/common.py:237-267, measured as measure_request at
+    :94-121): HF owns the cache; the whole prompt goes in one call; then one forced token per
+    call with logits_to_keep=1, each followed by the argmax and its host read. The prompt is the
+    GPU run's (seeded uniform random ids, same length) and is prefilled with all host threads as
+    untimed set-up; the forced decode tokens are seeded random ids."""
+    from xinfer_b200 import synthetic
+
+    all_threads = len(os.sched_getaffinity(0))
+    model = hf_eager_model(g)
+    prompt = synthetic.random_prompt(g, prompt_len, seed=1000)
+    forced = synthetic.random_prompt(g, (steps + warmup) * len(threads_list), seed=77)
+    rates = {}
+    with torch.inference_mode():
+        torch.set_num_threads(all_threads)
+        out = model(input_ids=torch.tensor([prompt]), past_key_values=None, use_cache=True,
+                    logits_to_keep=1)
+        cache = out.past_key_values
+        out.logits[:, -1, :].argmax(-1).item()
+        k = 0
+        for threads in threads_list:
+            torch.set_num_threads(threads)
+            times = []
+            for _ in range(warmup + steps):
+                t0 = time.perf_counter()
+                out = model(input_ids=torch.tensor([[forced[k]]]), past_key_values=cache,
+                            use_cache=True, logits_to_keep=1)
+                cache = out.past_key_values
+                out.logits[:, -1, :].argmax(-1).item()
+                times.append(time.perf_counter() - t0)
+                k += 1
+            rates[threads] = steps / sum(times[warmup:])
+    torch.set_num_threads(all_threads)
+    return rates, prompt_len + k
+
+
+def cpu_baseline(args, g, steps=8, warmup=2):
+    """The HF eager CPU baseline at the GPU run's context (all threads, then 1 thread)."""
+    threads = len(os.sched_getaffinity(0))
+    rates, end = hf_eager_baseline(g, max(1, args.prompt), steps, warmup, [threads, 1])
+    return {"value": rates[threads], "unit": UNIT, "cores": threads, "kind": "reference",
+            "value_1_thread": rates[1],
+            "sample": f"HF transformers eager {args.config} (bf16, sdpa, HF cache) on the CPU with the "
+                      f"call pattern of the reference's HF benchmark worker: a {args.prompt}-token "
+                      f"prompt in one call (untimed), then {warmup} + {steps} forced decode tokens "
+                      f"per thread count, one per call with logits_to_keep=1, argmax and host read "
+                      f"per step, contexts {args.prompt + 1}..{end}; value: {threads} threads; "
+                      f"value_1_thread: 1 thread (the reference's policy)"}
+
+
+def oracle_port_rate(args, g, budget_s):
     """The CPU oracle (port of the reference step) on this host: decode tokens of the same model
-    at a short context until the budget is spent."""
+    at a short context until the budget is spent (a secondary figure beside the HF baseline)."""
     from oracle import qwen_step as O
     from xinfer_b200 import synthetic
 
@@ -208,8 +289,13 @@ def cpu_baseline(args, g, budget_s):
         n += 1
     dt = time.perf_counter() - t0
     return {"value": n / dt, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{n} decode tokens of the CPU oracle at context 2..{n + 1}, fp32 torch on "
+            "sample": f"{n} decode tokens of the fp32 CPU oracle at context 2..{n + 1} on "
                       f"{threads} threads"}
+
+
+def hf_eager_baseline_one_thread(g, args, steps):
+    rates, end = hf_eager_baseline(g, max(1, args.prompt), steps, 1, [1])
+    return rates[1], end
 
 
 def run_reference(args):
@@ -219,16 +305,29 @@ def run_reference(args):
     from xinfer_b200 import configs
 
     g = configs.get(args.config)
-    res = cpu_baseline(args, g, budget_s=min(120.0, 4.0 * max(1, args.steps) ** 0.5 * 3))
+    # all host threads for the timed steps, then a shorter 1-thread sample (the reference's policy)
+    threads = len(os.sched_getaffinity(0))
+    steps, warmup = max(1, args.steps), max(1, args.warmup)
+    rates, end = hf_eager_baseline(g, max(1, args.prompt), steps, warmup, [threads])
+    one, _ = hf_eager_baseline_one_thread(g, args, min(steps, 4))
+    value = rates[threads]
+    res = {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "value_1_thread": one,
+           "sample": f"HF transformers eager {args.config} (bf16, sdpa, HF cache) on the CPU with the "
+                     f"call pattern of the reference's HF benchmark worker: a {args.prompt}-token "
+                     f"prompt in one call (untimed), then {warmup} + {steps} forced decode tokens, one "
+                     f"per call with logits_to_keep=1, argmax and host read per step, contexts "
+                     f"{args.prompt + 1}..{end}, {threads} threads; value_1_thread: 1 thread, "
+                     f"{min(steps, 4)} tokens after 1 warm-up"}
     line = {
-        "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / res["value"],
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": steps, "warmup": warmup, "ms_per_step": 1000.0 / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "impl": "reference",
-        "config": {"workload": workload(args) + " (CPU sample)", "model": args.config, "global_batch": 1,
-                   "seq_len": args.capacity, "parallelism": "cpu"},
+        "config": {"workload": workload(args) + " (HF eager on the CPU)", "model": args.config,
+                   "global_batch": 1, "seq_len": args.capacity, "prompt": args.prompt,
+                   "parallelism": "cpu"},
         "cpu_baseline": res,
-        "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -269,7 +368,7 @@ def main():
         gen = torch.Generator().manual_seed(4242 + rank)
         lengths = [int(x) for x in torch.randint(2, args.prompt + 1, (B,), generator=gen)]
     prompts = [synthetic.random_prompt(g, n, seed=1000 + 17 * b + rank) for b, n in enumerate(lengths)]
-    if max(lengths) + args.warmup + args.steps > args.capacity:  # each leg starts from a fresh prefill
+    if max(lengths) + args.warmup + args.steps + 1 > args.capacity:  # each leg starts from a fresh prefill
         raise SystemExit("prompt + steps exceed the KV capacity")
     stream = torch.cuda.current_stream(dev)
 
@@ -371,17 +470,22 @@ def main():
     if args.trace and rank == 0:
         from xinfer_b200 import _native as nat
 
+        # one more step after the e2e leg, at the bench's context, with the stage trace on
         buf = torch.zeros(nat.TRACE_BYTES // 8, dtype=torch.int64, device=dev)
         nat.check(nat.load().xb_debug_trace(buf.data_ptr(), nat.TRACE_BYTES))
-        runner.reset()
-        for t in range(min(64, max(lengths))):
-            runner.step_batch([[p_[t]] if t < len(p_) else [] for p_ in prompts])
+        eng.launch([int(t) for t in next_host[:B]], [s + total for s in starts],
+                   [s + total + 1 for s in starts], [1] * B, runner.state, runner.state,
+                   runner.logits, runner.next_tokens)
         torch.cuda.synchronize(dev)
         nat.check(nat.load().xb_debug_trace(None, 0))
         torch.save({"trace": buf.cpu(), "ncta": torch.cuda.get_device_properties(dev).multi_processor_count,
                     "stride": nat.TRACE_STRIDE, "stages": nat.TRACE_STAGES}, args.trace)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args, g, args.cpu_seconds)
+        eng.close()
+        del weights, runner
+        torch.cuda.empty_cache()
+        line["cpu_baseline"] = cpu_baseline(args, g)
+        line["cpu_baseline"]["oracle_port"] = oracle_port_rate(args, g, args.cpu_seconds)
     eng.close()
     if dist is not None:
         dist.barrier()

@@ -47,8 +47,32 @@ def prepare_weights(state_dict):
     return {k: v.float() for k, v in state_dict.items()}
 
 
+# Accumulation type of the linears. fp32 is the reference's (cuBLAS fp32 accumulation);
+# fp64 gives the "twin" oracle whose difference from the fp32 one measures how far two valid
+# summation orders drift apart on a given workload (the noise floor the GPU parity tests use).
+_LINEAR_ACC = torch.float32
+
+
+class accumulate(object):
+    """Context manager: run the oracle's linears with another accumulation dtype."""
+
+    def __init__(self, dtype):
+        self.dtype = dtype
+
+    def __enter__(self):
+        global _LINEAR_ACC
+        self.prev, _LINEAR_ACC = _LINEAR_ACC, self.dtype
+        return self
+
+    def __exit__(self, *exc):
+        global _LINEAR_ACC
+        _LINEAR_ACC = self.prev
+
+
 def linear(x, w):
     """bf16 linear: fp32 accumulate, bf16 output (cuBLAS GEMM as lowered by Inductor)."""
+    if _LINEAR_ACC is not torch.float32:
+        return rbf((x.to(_LINEAR_ACC) @ w.t().to(_LINEAR_ACC)).float())
     return rbf(x @ w.t())
 
 

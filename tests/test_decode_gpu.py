@@ -1,12 +1,18 @@
 """Parity of the CUDA decode megakernel (through the C ABI) with the CPU oracle and with the
 golden fixtures made from the reference's own step.
 
-Tolerances are the north-star bar: bf16 logits max-abs <= 2e-2 and cosine >= 0.9999 per step;
-recurrent / conv state relative L2 <= 1e-2; greedy argmax of the kernel equals torch.argmax of
-the kernel's own logits exactly. KV slot writes are bf16 roundings of fp32 GEMV sums whose
-reduction order differs from the reference's GEMM library, so the test reports the bitwise
-fraction and bounds it, and checks exactly that no slot outside [position] was written.
+Tolerances: the north-star bar (bf16 logits max-abs <= 2e-2 widened by one bf16 ulp of the
+reference value, cosine >= 0.9999, state relative L2 <= 1e-2) on shallow configurations, where a
+one-ulp flip of an fp32 sum cannot cascade; on full-depth models, twice the measured noise floor
+of that very schedule (tests/golden/noise_floor.json: the oracle with fp32 sums against its twin
+with fp64 sums), step by step. The fused argmax always equals torch.argmax of the kernel's own
+logits; greedy tokens equal the reference's or are near-ties inside the step's bound (the margin
+of every mismatch is checked). KV writes are checked exactly for their region (only the appended
+slot changes) and statistically for their values (tests/test_headline_gpu.py: bitwise fraction
+and ulp distances against the noise floor).
 """
+
+import json
 
 from pathlib import Path
 
@@ -22,10 +28,18 @@ pytestmark = pytest.mark.gpu
 LOGIT_MAX_ABS = 2e-2
 LOGIT_COS = 0.9999
 STATE_REL = 1e-2
-# full-depth random-init models sit at a measured bf16 noise floor (see tests/test_oracle.py)
-FULL_MAX_ABS = 0.15
-FULL_COS = 0.999
 GOLDEN = Path(__file__).resolve().parent / "golden"
+FLOOR = json.loads((GOLDEN / "noise_floor.json").read_text())
+
+
+def floor_bounds(per_step):
+    """(max-abs, cosine) bound per step: twice the running maximum of the twin difference, never
+    tighter than the north-star bar needs."""
+    out, mx, mc = [], 0.0, 0.0
+    for st in per_step:
+        mx, mc = max(mx, st["max_abs"]), max(mc, 1.0 - st["cosine"])
+        out.append((max(LOGIT_MAX_ABS, 2.0 * mx), min(LOGIT_COS, 1.0 - 2.0 * mc)))
+    return out
 
 _MODELS = {}
 
@@ -296,23 +310,110 @@ def test_matches_reference_fixtures(fixture, cuda_device):
     g, sd, W, eng = model(fx["config"], fx["capacity"], cuda_device, jitter=fx["jitter"], seed=fx["seed"])
     got, toks, state, _ = run_schedule_gpu(eng, g, fx["schedule"], cuda_device)
     summary = fx["logits_summary"]
+    floor = FLOOR["fixtures"].get(fixture)
+    bounds = floor_bounds(floor["per_step"]) if floor else None
+    tail = fx.get("logits_tail")
+    tail0 = len(fx["schedule"]) - (tail.shape[0] if tail is not None else 0)
     for s, tokens in enumerate(fx["schedule"]):
         for r, t in enumerate(tokens):
             if not t:
                 assert torch.count_nonzero(got[s, r]) == 0
                 continue
+            mine = int(torch.argmax(got[s, r].float()))
+            assert int(toks[s, r]) == mine, "fused argmax"
+            theirs = int(summary["argmax"][s, r])
             if fx["logits"] is not None:
-                check_logits(got[s, r], fx["logits"][s, r], f"{fixture} step {s} row {r}")
+                ref = fx["logits"][s, r]
+                check_logits(got[s, r], ref, f"{fixture} step {s} row {r}")
+                margin = float(ref[theirs].float() - ref[mine].float())
+                assert mine == theirs or margin <= LOGIT_MAX_ABS, (s, r, mine, theirs, margin)
+                continue
+            bmax, bcos = bounds[s]
+            if tail is not None and s >= tail0:
+                ref = tail[s - tail0, r].float()
+                row = got[s, r].float().cpu()
+                err, cos = (row - ref).abs().max().item(), O.cosine(row, ref)
+                assert err <= bmax and cos >= bcos, f"{fixture} step {s}: max abs {err}, cosine {cos}"
+                margin = float(ref[theirs] - ref[mine])
             else:
                 idx = summary["top_indices"][s, r]
                 vals = got[s, r].float().cpu()[idx]
                 err = (vals - summary["top_values"][s, r].float()).abs().max().item()
-                assert err <= FULL_MAX_ABS, f"{fixture} step {s}: top-32 logits differ by {err}"
+                assert err <= bmax, f"{fixture} step {s}: top-32 logits differ by {err}"
                 sl = got[s, r, ::97].float().cpu()
                 ref = summary["stride_slice"][s, r].float()
-                assert O.cosine(sl, ref) >= FULL_COS
-                assert (sl - ref).abs().max().item() <= FULL_MAX_ABS
-    rel = STATE_REL if fx["logits"] is not None else 5 * STATE_REL
+                assert O.cosine(sl, ref) >= bcos and (sl - ref).abs().max().item() <= bmax
+                hit = (idx == mine).nonzero()
+                margin = (float(summary["top_values"][s, r, 0] - summary["top_values"][s, r, int(hit[0])])
+                          if len(hit) else float("inf"))
+            assert mine == theirs or margin <= bmax, f"{fixture} step {s}: token {mine} vs {theirs}, margin {margin}"
+    if floor:
+        rel = max(STATE_REL, 2 * floor["recurrent_rel_l2_max"], 2 * floor["conv_rel_l2_max"],
+                  2 * floor.get("kv_rel_l2", 0.0))
+    else:
+        rel = STATE_REL
     for i, smp in enumerate(fx["state_sample"]):
         a = state[i].reshape(-1)[smp["index"].long().to(cuda_device)].float().cpu()
         assert O.rel_l2(a, smp["value"].float()) <= rel, f"{fixture} state {i}"
+
+
+def test_qwen3_4000_token_prefix_full_width(cuda_device):
+    """Qwen3-0.6B widths (16 q / 8 KV heads, 151936 vocabulary), two layers, a 4000-slot random
+    KV prefix, then four teacher-forced steps at positions 3999..4002: the split-KV partials and
+    their combine at the long-context benchmark's length."""
+    cap, L = 4096, 3999
+    g, sd, W, eng = model("qwen3-0.6b-l2", cap, cuda_device, jitter=0.1)
+    full = eng.allocate_state()
+    gen = torch.Generator().manual_seed(21)
+    cpu_state = []
+    for t in full:
+        v = (torch.randn(t.shape[1:], generator=gen) * 0.5).to(t.dtype)
+        v[:, L:] = 0
+        t[0].copy_(v)
+        cpu_state.append(v[None].clone())
+    state = [t.narrow(0, 0, 1) for t in full]
+    gen = torch.Generator().manual_seed(22)
+    for k in range(4):
+        tok = int(torch.randint(0, g.vocab, (1,), generator=gen))
+        pos = L + k
+        nxt = torch.empty(1, dtype=torch.int64, device=cuda_device)
+        logits = eng.decode_step(torch.tensor([[tok]], dtype=torch.int64, device=cuda_device),
+                                 torch.tensor([[pos]], dtype=torch.int64, device=cuda_device), state,
+                                 torch.tensor([pos + 1], dtype=torch.int32),
+                                 torch.tensor([1], dtype=torch.int32), next_tokens=nxt)
+        eng.check_device_error()
+        want, cpu_state = O.decode_step(g, W, [tok], [pos], cpu_state, [pos + 1], [1])
+        check_logits(logits[0], want[0], f"qwen3-0.6b-l2 position {pos}", cos_min=FULLW_COS,
+                     max_abs=FULLW_MAX_ABS)
+        assert int(nxt[0]) == int(torch.argmax(logits[0].float()))
+    for a, b in zip(state, cpu_state):
+        n = L + 4
+        assert O.rel_l2(a[:, :, :n].float().cpu(), b[:, :, :n].float()) <= STATE_REL
+
+
+def test_batch8_long_ragged_schedule(cuda_device):
+    """64 steps of eight rows through the tensor-core tiles: rows join late, go idle and come
+    back, so KV lengths stay ragged; every active row is compared with the oracle every step."""
+    g, sd, W, eng = model("qwen3.5-tiny", 80, cuda_device)
+    gen = torch.Generator().manual_seed(31)
+    sched = []
+    for s in range(64):
+        row = []
+        for r in range(8):
+            active = (s >= r) and ((s + 3 * r) % 7 != 0)
+            row.append([int(torch.randint(0, g.vocab, (1,), generator=gen))] if active or s == 0 else [])
+        sched.append(row)
+    got, toks, state, full = run_schedule_gpu(eng, g, sched, cuda_device)
+    want, ostate = run_schedule_oracle(g, W, sched, 80)
+    for s, tokens in enumerate(sched):
+        for r, t in enumerate(tokens):
+            if t:
+                check_logits(got[s, r], want[s, r], f"batch-8 step {s} row {r}")
+                assert int(toks[s, r]) == int(torch.argmax(got[s, r].float()))
+            else:
+                assert torch.count_nonzero(got[s, r]) == 0
+    for i, (a, b) in enumerate(zip(state, ostate)):
+        a, b = a.float().cpu(), b.float()
+        if not g.is_delta(i // 2):
+            a, b = a[:, :, :64], b[:, :, :64]
+        assert O.rel_l2(a, b) <= STATE_REL, f"state {i}"

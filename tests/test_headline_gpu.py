@@ -1,0 +1,127 @@
+"""Parity of the CUDA decode step on the benchmarked workloads, against the CPU oracle.
+
+Headline: full-depth Qwen3.5-0.8B (seeded random-init bf16 weights), KV capacity 4096, a
+512-token uniform random prompt fed one token per step through Engine.decode_step (the
+reference's ModelStep.forward contract), then 8 more teacher-forced decode steps: 520 steps,
+each compared with the oracle on identical inputs.
+
+Bounds. Over 24 random-init layers two valid fp32 summation orders drift apart: the oracle with
+fp32 sums and its twin with fp64 sums differ step by step by the figures recorded in
+tests/golden/noise_floor.json (made by tests/golden/measure_floor.py). Step s is held to twice
+the largest twin difference of steps 0..s, and never looser than needed
+(max-abs 2e-2, cosine 0.9999, state rel-L2 1e-2) wherever the floor is below it. Greedy tokens
+must equal the oracle's or be a near-tie inside that step's bound; the fused argmax must equal
+torch.argmax of the kernel's own logits on every step. KV slots are compared element by element:
+bitwise fraction, fraction within 1 and 2 bf16 ulps, relative L2, against the same twin figures.
+
+Set XB_PARITY_REPORT=<path> to write the per-step figures as JSON.
+"""
+
+import json
+import os
+from pathlib import Path
+
+import pytest
+import torch
+
+from oracle import qwen_step as O
+from xinfer_b200 import configs, synthetic
+from xinfer_b200.engine import Engine
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+FLOOR = json.loads((GOLDEN / "noise_floor.json").read_text())
+LOGIT_MAX_ABS, LOGIT_COS, STATE_REL = 2e-2, 0.9999, 1e-2
+# the headline workload (must agree with the record of the floor measurement)
+CONFIG, CAPACITY, PROMPT, DECODE, PROMPT_SEED, DECODE_SEED = "qwen3.5-0.8b", 4096, 512, 8, 2024, 2025
+
+
+def step_bounds(per_step):
+    """(max-abs, cosine) bound of every step: twice the running maximum of the twin difference,
+    and at least as tight as the north-star bar would allow."""
+    out, mx, mc = [], 0.0, 0.0
+    for st in per_step:
+        mx, mc = max(mx, st["max_abs"]), max(mc, 1.0 - st["cosine"])
+        out.append((max(LOGIT_MAX_ABS, 2.0 * mx), min(LOGIT_COS, 1.0 - 2.0 * mc)))
+    return out
+
+
+def bf16_ulps(a, b):
+    def ordered(t):
+        i = t.contiguous().view(torch.int16).int()
+        return torch.where(i < 0, -(i & 0x7FFF), i)
+    return (ordered(a) - ordered(b)).abs()
+
+
+def kv_figures(got, want):
+    u = bf16_ulps(got, want).flatten()
+    return {"kv_bitwise_fraction": float((u == 0).float().mean()),
+            "kv_within_1ulp": float((u <= 1).float().mean()),
+            "kv_within_2ulp": float((u <= 2).float().mean()),
+            "kv_max_ulp": int(u.max()),
+            "kv_rel_l2": O.rel_l2(got.float(), want.float())}
+
+
+def test_headline_workload_matches_oracle(cuda_device):
+    head = FLOOR["headline"]
+    assert (head["config"], head["capacity"], head["prompt"], head["decode"], head["prompt_seed"],
+            head["decode_seed"]) == (CONFIG, CAPACITY, PROMPT, DECODE, PROMPT_SEED, DECODE_SEED)
+    g = configs.get(CONFIG)
+    sd = synthetic.make_state_dict(g, seed=0)
+    W = O.prepare_weights(sd)
+    eng = Engine(g, {k: v.to(cuda_device) for k, v in sd.items()}, capacity=CAPACITY, device=cuda_device)
+    del sd
+    tokens = (synthetic.random_prompt(g, PROMPT, seed=PROMPT_SEED)
+              + synthetic.random_prompt(g, DECODE, seed=DECODE_SEED))
+    bounds = step_bounds(head["per_step"])
+    state = [t.narrow(0, 0, 1) for t in eng.allocate_state()]
+    ostate = O.allocate_state(g, CAPACITY, rows=1)
+    nxt = torch.empty(1, dtype=torch.int64, device=cuda_device)
+    steps, mismatches = [], []
+    for pos, tok in enumerate(tokens):
+        ids = torch.tensor([[tok]], dtype=torch.int64, device=cuda_device)
+        cp = torch.tensor([[pos]], dtype=torch.int64, device=cuda_device)
+        out = eng.decode_step(ids, cp, state, torch.tensor([pos + 1], dtype=torch.int32),
+                              torch.tensor([1], dtype=torch.int32), next_tokens=nxt)
+        logits, *state = out
+        want, ostate = O.decode_step(g, W, [tok], [pos], ostate, [pos + 1], [1])
+        got = logits[0].float().cpu()
+        ref = want[0].float()
+        err, cos = (got - ref).abs().max().item(), O.cosine(got, ref)
+        mine, theirs = int(torch.argmax(got)), int(torch.argmax(ref))
+        assert int(nxt[0]) == mine, f"step {pos}: fused argmax differs from torch.argmax"
+        margin = float(ref[theirs] - ref[mine])
+        steps.append({"max_abs": err, "cosine": cos, "argmax_equal": mine == theirs})
+        if mine != theirs:
+            mismatches.append({"step": pos, "ours": mine, "oracle": theirs, "margin": margin})
+        bmax, bcos = bounds[pos]
+        assert err <= bmax and cos >= bcos, f"step {pos}: max abs {err} (bound {bmax}), cosine {cos} (bound {bcos})"
+        assert mine == theirs or margin <= bmax, f"step {pos}: greedy token differs by margin {margin}"
+    eng.check_device_error()
+    n = len(tokens)
+    rec, conv, kv_got, kv_want = [], [], [], []
+    for i in range(g.num_layers):
+        a0, a1 = state[2 * i].cpu(), state[2 * i + 1].cpu()
+        if g.is_delta(i):
+            conv.append(O.rel_l2(a0.float(), ostate[2 * i].float()))
+            rec.append(O.rel_l2(a1, ostate[2 * i + 1]))
+        else:
+            for a, b in ((a0, ostate[2 * i]), (a1, ostate[2 * i + 1])):
+                assert torch.count_nonzero(a[:, :, n:]) == 0, "KV written beyond the fed positions"
+                kv_got.append(a[:, :, :n].flatten())
+                kv_want.append(b[:, :, :n].flatten())
+    kv = kv_figures(torch.cat(kv_got), torch.cat(kv_want))
+    report = {"steps": steps, "argmax_mismatches": mismatches, "recurrent_rel_l2_max": max(rec),
+              "conv_rel_l2_max": max(conv), **kv,
+              "max_abs_all": max(s["max_abs"] for s in steps),
+              "min_cosine_all": min(s["cosine"] for s in steps)}
+    if os.environ.get("XB_PARITY_REPORT"):
+        Path(os.environ["XB_PARITY_REPORT"]).write_text(json.dumps(report, indent=1) + "\n")
+    assert len(mismatches) <= max(2, 2 * head["argmax_disagreements"])
+    assert max(rec) <= max(STATE_REL, 2 * head["recurrent_rel_l2_max"])
+    assert max(conv) <= max(STATE_REL, 2 * head["conv_rel_l2_max"])
+    assert kv["kv_rel_l2"] <= max(STATE_REL, 2 * head["kv_rel_l2"])
+    assert kv["kv_within_2ulp"] >= head["kv_within_2ulp"] - 0.05
+    assert kv["kv_bitwise_fraction"] >= head["kv_bitwise_fraction"] / 2
+    eng.close()

@@ -2,6 +2,7 @@
 (tests/golden/make_golden.py) and against the known-answer cases of the reference's tests."""
 
 import hashlib
+import json
 from pathlib import Path
 
 import numpy as np
@@ -73,31 +74,57 @@ def test_oracle_matches_reference_fixture(name):
         assert frac >= 0.999, f"layer-0 conv state bitwise fraction {frac}"
 
 
-# Full-depth random-init models amplify a single one-ulp bf16 flip (any fp32 reduction order)
-# to ~1.6% of the final hidden state over 28 layers: two valid accumulation orders of this very
-# oracle (fp32 vs fp64 GEMV sums) differ by max-abs 0.037 / cosine 0.99992 after three Qwen3-0.6B
-# steps and by max-abs 0.086 / cosine 0.99957 already at the first Qwen3.5-0.8B step. Full-depth
-# runs are held to that measured noise floor (with margin); the north-star bar (2e-2, 0.9999)
-# applies to the shallow configs, where a flip cannot cascade.
-FULL_MAX_ABS = 0.15
-FULL_COS = 0.999
+# Full-depth random-init models amplify a single one-ulp bf16 flip of any fp32 sum: two valid
+# accumulation orders of this very oracle (fp32 against fp64 sums in every linear) drift apart
+# step by step by the figures of tests/golden/noise_floor.json (tests/golden/measure_floor.py).
+# The oracle is held to twice that floor against the reference's full-depth fixtures, step by
+# step; the north-star bar (2e-2, 0.9999) applies wherever the floor is below it.
+FLOOR = json.loads((GOLDEN / "noise_floor.json").read_text())
+
+
+def floor_bounds(per_step):
+    out, mx, mc = [], 0.0, 0.0
+    for st in per_step:
+        mx, mc = max(mx, st["max_abs"]), max(mc, 1.0 - st["cosine"])
+        out.append((max(LOGIT_MAX_ABS, 2.0 * mx), min(LOGIT_COS, 1.0 - 2.0 * mc)))
+    return out
 
 
 @pytest.mark.parametrize("name", [f for f in FIXTURES if "0.6b" in f or "0.8b" in f])
 def test_oracle_matches_full_size_fixture(name):
     fx = torch.load(GOLDEN / f"{name}.pt", weights_only=False)
     g, logits, state, _ = run_oracle(fx)
+    floor = FLOOR["fixtures"][name]
+    bounds = floor_bounds(floor["per_step"])
     summ = fx["logits_summary"]
+    tail = fx.get("logits_tail")
+    tail0 = len(fx["schedule"]) - (tail.shape[0] if tail is not None else 0)
     for s in range(len(fx["schedule"])):
+        bmax, bcos = bounds[s]
         idx = summ["top_indices"][s, 0]
         err = (logits[s, 0].float()[idx] - summ["top_values"][s, 0].float()).abs().max().item()
-        assert err <= FULL_MAX_ABS
+        assert err <= bmax, (s, err, bmax)
         sl = logits[s, 0, ::97].float()
-        assert O.cosine(sl, summ["stride_slice"][s, 0]) >= FULL_COS
-        assert (sl - summ["stride_slice"][s, 0].float()).abs().max().item() <= FULL_MAX_ABS
+        assert O.cosine(sl, summ["stride_slice"][s, 0]) >= bcos
+        assert (sl - summ["stride_slice"][s, 0].float()).abs().max().item() <= bmax
+        if tail is not None and s >= tail0:
+            a, b = logits[s, 0].float(), tail[s - tail0, 0].float()
+            assert (a - b).abs().max().item() <= bmax and O.cosine(a, b) >= bcos, s
+            mine, theirs = int(a.argmax()), int(b.argmax())
+            assert mine == theirs or float(b[theirs] - b[mine]) <= bmax, (s, mine, theirs)
+    rel = max(STATE_REL, 2 * floor["recurrent_rel_l2_max"], 2 * floor["conv_rel_l2_max"],
+              2 * floor.get("kv_rel_l2", 0.0))
     for i, smp in enumerate(fx["state_sample"]):
         got = state[i].reshape(-1)[smp["index"].long()]
-        assert O.rel_l2(got.float(), smp["value"].float()) <= 5 * STATE_REL, i
+        assert O.rel_l2(got.float(), smp["value"].float()) <= rel, i
+
+
+def test_noise_floor_record_matches_its_workload():
+    """The floor record names the workload the headline GPU test runs."""
+    head = FLOOR["headline"]
+    assert (head["config"], head["capacity"], head["prompt"], head["decode"]) == ("qwen3.5-0.8b", 4096, 512, 8)
+    assert len(head["per_step"]) == head["prompt"] + head["decode"]
+    assert set(FLOOR["fixtures"]) >= {f for f in FIXTURES if "0.6b" in f or "0.8b" in f}
 
 
 def test_attention_lower_right_causality_kat():

@@ -392,6 +392,14 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], unsigned a0, unsigned a
 }
 #endif
 
+#ifndef XB_POLL_NS
+#define XB_POLL_NS 0
+#endif
+// Pause between two polls of a word that was not ready yet (0: poll back to back).
+__device__ __forceinline__ void poll_pause() {
+  if (XB_POLL_NS) __nanosleep(XB_POLL_NS);
+}
+
 // ---- waits (free functions: the consumer object must never have its address taken, so that
 // its state stays in registers) -------------------------------------------------------------
 // True when a wait must end: this CTA aborted, or (only after kSlowWaitNs of waiting, so that the
@@ -414,6 +422,7 @@ static __device__ __noinline__ uint4 repoll4(const unsigned *w, unsigned tg, vol
   uint4 v;
   uint64_t t0 = 0;
   for (unsigned spins = 1;; ++spins) {
+    poll_pause();
     v = ld_poll_u4(w);
     if (tag4_ok(v, tg)) break;
     if ((spins & 15u) == 0 && wait_give_up(abort_flag, ctrl, t0)) break;
@@ -425,6 +434,7 @@ static __device__ __noinline__ unsigned repoll1(const unsigned *w, unsigned tg, 
   unsigned v;
   uint64_t t0 = 0;
   for (unsigned spins = 1;; ++spins) {
+    poll_pause();
     v = ld_poll_u32(w);
     if ((v >> 16) == tg) break;
     if ((spins & 15u) == 0 && wait_give_up(abort_flag, ctrl, t0)) break;
@@ -436,6 +446,7 @@ static __device__ __noinline__ ulonglong2 repoll2f(const u64 *w, unsigned tg, vo
   ulonglong2 v;
   uint64_t t0 = 0;
   for (unsigned spins = 1;; ++spins) {
+    poll_pause();
     v = ld_poll_u64x2(w);
     if (ftag_tag(v.x) == tg && ftag_tag(v.y) == tg) break;
     if ((spins & 15u) == 0 && wait_give_up(abort_flag, ctrl, t0)) break;
@@ -447,6 +458,7 @@ static __device__ __noinline__ float repoll1f(const u64 *w, unsigned tg, volatil
   u64 v;
   uint64_t t0 = 0;
   for (unsigned spins = 1;; ++spins) {
+    poll_pause();
     v = ld_poll_u64(w);
     if (ftag_tag(v) == tg) break;
     if ((spins & 15u) == 0 && wait_give_up(abort_flag, ctrl, t0)) break;
@@ -555,6 +567,7 @@ template <int NB> struct Consumer {
     for (int i = 0; i < N; ++i) late |= want(i) && !ok(v[i]);
     uint64_t t0 = 0;
     for (unsigned round = 1; late; ++round) {
+      poll_pause();
 #pragma unroll
       for (int i = 0; i < N; ++i)
         if (want(i) && !ok(v[i])) v[i] = ld_poll_u4(addr(i));
@@ -571,6 +584,7 @@ template <int NB> struct Consumer {
     for (int i = 0; i < N; ++i) late |= want(i) && (v[i] >> 16) != tg;
     uint64_t t0 = 0;
     for (unsigned round = 1; late; ++round) {
+      poll_pause();
 #pragma unroll
       for (int i = 0; i < N; ++i)
         if (want(i) && (v[i] >> 16) != tg) v[i] = ld_poll_u32(addr(i));
@@ -590,6 +604,7 @@ template <int NB> struct Consumer {
     for (int i = 0; i < N; ++i) late |= want(i) && !ok(v[i]);
     uint64_t t0 = 0;
     for (unsigned round = 1; late; ++round) {
+      poll_pause();
 #pragma unroll
       for (int i = 0; i < N; ++i)
         if (want(i) && !ok(v[i])) v[i] = ld_poll_u64x2(addr(i));
@@ -889,33 +904,53 @@ template <int NB> struct Consumer {
 #if !XB_TENSOR_TILES
   // Gated RMSNorm of the DeltaNet core output (HF Qwen3_5RMSNormGated, as called in
   // compiler/qwen35/adapters/delta.py:46-47): y = bf16( bf16(w * bf16(x * r)) * silu(z) ).
-  // Each thread derives its head's 1/rms from the eight per-tile partial sums itself.
+  // One warp covers one head (32 lanes x 4 values) per chunk index; lanes 0..3 load the head's
+  // eight per-tile sums of squares (two per lane) and the warp reduces them as
+  // ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)). All loads of a row are issued together
+  // and only late words are loaded again.
   __device__ void gated_norm_prologue(const bf16 *w, unsigned tg) {
     uint2 *act = reinterpret_cast<uint2 *>(U);
     const int K = p.HV * p.DK, nq = K / 4, DK = p.DK;
     const int zoff = 2 * p.HK * p.DK + p.HV * p.DK;
     constexpr int MAXC = 4;  // K <= 4 * 256 * 4
+    uint2 wq[MAXC];
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i)
+      wq[i] = tid + i * kCT < nq ? *reinterpret_cast<const uint2 *>(w + ((tid + i * kCT) * 4) % DK)
+                                 : make_uint2(0, 0);
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
+      uint4 xz[2 * MAXC];  // core chunks, then gate (z) chunks
+      ulonglong2 sv[MAXC];
+      auto addr = [&](int k) {
+        const int c = tid + (k % MAXC) * kCT;
+        return k < MAXC ? p.core + (size_t)b * K + c * 4 : p.proj + (size_t)b * p.pstride + zoff + c * 4;
+      };
+      auto want = [&](int k) { return tid + (k % MAXC) * kCT < nq && b < p.B; };
+      auto saddr = [&](int i) {
+        const int h = ((tid + i * kCT) * 4) / DK;
+        return p.ssq + ((size_t)b * p.HV + h) * 8 + 2 * (lane & 3);
+      };
+      auto swant = [&](int i) { return tid + i * kCT < nq && b < p.B && lane < 4; };
+#pragma unroll
+      for (int k = 0; k < 2 * MAXC; ++k) xz[k] = want(k) ? ldcg_u4(addr(k)) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) sv[i] = swant(i) ? ldcg_u64x2(saddr(i)) : make_ulonglong2(0, 0);
+      settle(xz, addr, want, [&](const uint4 &v) { return tag4_ok(v, tg); });
+      settle64(sv, saddr, swant, tg);
 #pragma unroll
       for (int i = 0; i < MAXC; ++i) {
         const int c = tid + i * kCT;
+        float part = lane < 4 ? ftag_val(sv[i].x) + ftag_val(sv[i].y) : 0.f;
+        part += __shfl_xor_sync(0xffffffffu, part, 1);
+        part += __shfl_xor_sync(0xffffffffu, part, 2);
+        const float tot = __shfl_sync(0xffffffffu, part, 0);
         if (c >= nq) continue;
         uint2 o = make_uint2(0, 0);
         if (b < p.B) {
-          const uint4 xv = poll4(p.core + (size_t)b * K + c * 4, tg);
-          const uint4 zv = poll4(p.proj + (size_t)b * p.pstride + zoff + c * 4, tg);
-          const uint2 wv = *reinterpret_cast<const uint2 *>(w + (c * 4) % DK);
-          const int h = (c * 4) / DK;
-          const u64 *ps = p.ssq + ((size_t)b * p.HV + h) * 8;
-          float tot = 0.f;
-#pragma unroll
-          for (int t = 0; t < 8; t += 2) {
-            const ulonglong2 q = poll2f(ps + t, tg);
-            tot += ftag_val(q.x);
-            tot += ftag_val(q.y);
-          }
           const float r = rsqrtf(tot / (float)DK + p.eps);
+          const uint4 xv = xz[i], zv = xz[MAXC + i];
+          const uint2 wv = wq[i];
           const float x[4] = {bf_lo(xv.x), bf_lo(xv.y), bf_lo(xv.z), bf_lo(xv.w)};
           const float z[4] = {bf_lo(zv.x), bf_lo(zv.y), bf_lo(zv.z), bf_lo(zv.w)};
           const float wf[4] = {bf_lo(wv.x), bf_hi(wv.x), bf_lo(wv.y), bf_hi(wv.y)};
@@ -1093,6 +1128,7 @@ template <int NB> struct Consumer {
     case EPI_GATEUP: tile_loop<true, EPI_GATEUP>(g, lo, hi, otag); break;
     default: tile_loop<false, EPI_LOGITS>(g, lo, hi, otag); break;
     }
+    trace_mark(2);
     if (epi == EPI_RESID) h_ready = true;
     if (epi == EPI_LOGITS) {
       if (p.trace && tid == 0) p.trace[(size_t)blockIdx.x * kTraceStride + 3 * kTraceStages + 7] = globaltimer();
@@ -1453,6 +1489,7 @@ template <int NB> struct Consumer {
 #pragma unroll
       for (int k = 0; k < 3; ++k) xw[k] = xwant(k) ? ld_poll_u32(xaddr(k)) : 0u;
       settle1(xw, xaddr, xwant, tg);
+      trace_mark(1);
       const float xq = bf_lo(xw[0]);
       const float xv = tid < 16 ? bf_lo(xw[1]) : 0.f;
       if (warp == 0 && lane < 2) gsc = bf_lo(xw[2]);  // b, a
@@ -1624,6 +1661,7 @@ template <int NB> struct Consumer {
           }
       }
       csync();
+      trace_mark(1);
       bf16 *kc = kc_all + (((size_t)b * HKV + kvh) * p.C) * D;
       bf16 *vc = vc_all + (((size_t)b * HKV + kvh) * p.C) * D;
       // KV append (compiler/common/kernels/kv_cache.py:8-42): the s == 0 item writes slot pos.
@@ -1686,6 +1724,7 @@ template <int NB> struct Consumer {
           if (e < EPL) o[e] = fmaf(pb, vf[e], o[e] * corr);
         m = mn;
       }
+      trace_mark(2);
       // merge the P partial states of each head
       const int MS = D + 2;
       float *mw = mg + (size_t)warp * MS;
@@ -1749,6 +1788,7 @@ template <int NB> struct Consumer {
         ls[s] = ftag_val(v.y);
       }
       csync();
+      trace_mark(1);
       float M = -INFINITY;
       for (int s = 0; s < splits; ++s) M = fmaxf(M, ms[s]);
       float O = 0.f, Lw = 0.f;
