@@ -1,9 +1,12 @@
-"""Build the in-tree CUDA library (sm_100a) with nvcc.
+"""Build the in-tree libraries.
 
     python -m xinfer_b200.build [--force]
 
-Produces xinfer_b200/libxinfer_b200.so from xinfer_b200/csrc/*.cu. The library is plain C ABI
-(include/xinfer_b200.h) linked against the CUDA runtime only; torch is not needed to build it.
+  * xinfer_b200/libxinfer_b200.so from xinfer_b200/csrc/*.cu with nvcc for sm_100a: the plain C
+    ABI of include/xinfer_b200.h, linked against the CUDA runtime only (no torch);
+  * xinfer_b200/libxinfer_b200_ops.so from xinfer_b200/csrc/torch_ops.cpp with the host C++
+    compiler: the xinfer::qwen3_decode_step / qwen35_decode_step torch operators and their
+    AOTInductor C shims, linked against libtorch and libxinfer_b200.so (found next to it).
 """
 
 import argparse
@@ -18,6 +21,8 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 OUT = PKG / "libxinfer_b200.so"
+OPS_SRC = CSRC / "torch_ops.cpp"
+OPS_OUT = PKG / "libxinfer_b200_ops.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
@@ -33,6 +38,36 @@ def nvcc():
 
 def sources():
     return sorted(CSRC.glob("*.cu"))
+
+
+def torch_flags():
+    import torch
+    from torch.utils import cpp_extension
+
+    inc = cpp_extension.include_paths(device_type="cuda")
+    lib = cpp_extension.library_paths(device_type="cuda")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    flags = [f"-I{p}" for p in inc] + [f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_API_INCLUDE_EXTENSION_H"]
+    libs = [f"-L{p}" for p in lib] + [f"-Wl,-rpath,{p}" for p in lib]
+    libs += ["-lc10", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-lc10_cuda", "-L/usr/local/cuda/lib64",
+             "-lcudart"]
+    return flags, libs
+
+
+def build_ops(force=False):
+    """The torch operator library (host C++ only; the kernels stay in libxinfer_b200.so)."""
+    if not force and OPS_OUT.exists() and OPS_OUT.stat().st_mtime >= max(
+            OPS_SRC.stat().st_mtime, OUT.stat().st_mtime, (INCLUDE / "xinfer_b200.h").stat().st_mtime):
+        return OPS_OUT
+    flags, libs = torch_flags()
+    cxx = shutil.which("g++") or "c++"
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", *flags, f"-I{INCLUDE}", "-o", str(OPS_OUT) + ".tmp",
+           str(OPS_SRC), f"-L{PKG}", "-lxinfer_b200", "-Wl,-rpath,$ORIGIN", *libs]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(f"g++ failed:\n{' '.join(cmd)}\n{proc.stdout}{proc.stderr}")
+    os.replace(str(OPS_OUT) + ".tmp", OPS_OUT)
+    return OPS_OUT
 
 
 def headers():
@@ -69,6 +104,7 @@ def main():
     args = ap.parse_args()
     out = build(force=args.force, verbose=args.verbose)
     print(out)
+    print(build_ops(force=args.force))
 
 
 if __name__ == "__main__":
