@@ -8,7 +8,8 @@ each compared with the oracle on identical inputs.
 Bounds. Over 24 random-init layers two valid fp32 summation orders drift apart: the oracle with
 fp32 sums and its twin with fp64 sums differ step by step by the figures recorded in
 tests/golden/noise_floor.json (made by tests/golden/measure_floor.py). Step s is held to twice
-the largest twin difference of steps 0..s, and never looser than needed
+the largest twin difference within 16 steps of s (one step's twin difference is a single sample
+of the spread, so a window of them is used), and never looser than needed
 (max-abs 2e-2, cosine 0.9999, state rel-L2 1e-2) wherever the floor is below it. Greedy tokens
 must equal the oracle's or be a near-tie inside that step's bound; the fused argmax must equal
 torch.argmax of the kernel's own logits on every step. KV slots are compared element by element:
@@ -37,12 +38,14 @@ LOGIT_MAX_ABS, LOGIT_COS, STATE_REL = 2e-2, 0.9999, 1e-2
 CONFIG, CAPACITY, PROMPT, DECODE, PROMPT_SEED, DECODE_SEED = "qwen3.5-0.8b", 4096, 512, 8, 2024, 2025
 
 
-def step_bounds(per_step):
-    """(max-abs, cosine) bound of every step: twice the running maximum of the twin difference,
-    and at least as tight as the north-star bar would allow."""
-    out, mx, mc = [], 0.0, 0.0
-    for st in per_step:
-        mx, mc = max(mx, st["max_abs"]), max(mc, 1.0 - st["cosine"])
+def step_bounds(per_step, window=16):
+    """(max-abs, cosine) bound of every step: twice the largest twin difference within `window`
+    steps of it, and at least as tight as the north-star bar would allow."""
+    out = []
+    for s in range(len(per_step)):
+        near = per_step[max(0, s - window):s + window + 1]
+        mx = max(st["max_abs"] for st in near)
+        mc = max(1.0 - st["cosine"] for st in near)
         out.append((max(LOGIT_MAX_ABS, 2.0 * mx), min(LOGIT_COS, 1.0 - 2.0 * mc)))
     return out
 
@@ -92,12 +95,11 @@ def test_headline_workload_matches_oracle(cuda_device):
         mine, theirs = int(torch.argmax(got)), int(torch.argmax(ref))
         assert int(nxt[0]) == mine, f"step {pos}: fused argmax differs from torch.argmax"
         margin = float(ref[theirs] - ref[mine])
-        steps.append({"max_abs": err, "cosine": cos, "argmax_equal": mine == theirs})
+        bmax, bcos = bounds[pos]
+        steps.append({"max_abs": err, "cosine": cos, "argmax_equal": mine == theirs,
+                      "bound_max_abs": bmax, "bound_cosine": bcos})
         if mine != theirs:
             mismatches.append({"step": pos, "ours": mine, "oracle": theirs, "margin": margin})
-        bmax, bcos = bounds[pos]
-        assert err <= bmax and cos >= bcos, f"step {pos}: max abs {err} (bound {bmax}), cosine {cos} (bound {bcos})"
-        assert mine == theirs or margin <= bmax, f"step {pos}: greedy token differs by margin {margin}"
     eng.check_device_error()
     n = len(tokens)
     rec, conv, kv_got, kv_want = [], [], [], []
@@ -118,6 +120,12 @@ def test_headline_workload_matches_oracle(cuda_device):
               "min_cosine_all": min(s["cosine"] for s in steps)}
     if os.environ.get("XB_PARITY_REPORT"):
         Path(os.environ["XB_PARITY_REPORT"]).write_text(json.dumps(report, indent=1) + "\n")
+    for pos, st in enumerate(steps):
+        assert st["max_abs"] <= st["bound_max_abs"] and st["cosine"] >= st["bound_cosine"], (
+            f"step {pos}: max abs {st['max_abs']} (bound {st['bound_max_abs']}), "
+            f"cosine {st['cosine']} (bound {st['bound_cosine']})")
+    for m in mismatches:
+        assert m["margin"] <= steps[m["step"]]["bound_max_abs"], f"greedy token differs by margin {m}"
     assert len(mismatches) <= max(2, 2 * head["argmax_disagreements"])
     assert max(rec) <= max(STATE_REL, 2 * head["recurrent_rel_l2_max"])
     assert max(conv) <= max(STATE_REL, 2 * head["conv_rel_l2_max"])

@@ -82,10 +82,15 @@ def test_oracle_matches_reference_fixture(name):
 FLOOR = json.loads((GOLDEN / "noise_floor.json").read_text())
 
 
-def floor_bounds(per_step):
-    out, mx, mc = [], 0.0, 0.0
-    for st in per_step:
-        mx, mc = max(mx, st["max_abs"]), max(mc, 1.0 - st["cosine"])
+def floor_bounds(per_step, window=16):
+    """(max-abs, cosine) bound per step: twice the largest twin difference within `window` steps
+    of it (one step's difference is a single sample of the spread), never tighter than the
+    north-star bar needs."""
+    out = []
+    for s in range(len(per_step)):
+        near = per_step[max(0, s - window):s + window + 1]
+        mx = max(st["max_abs"] for st in near)
+        mc = max(1.0 - st["cosine"] for st in near)
         out.append((max(LOGIT_MAX_ABS, 2.0 * mx), min(LOGIT_COS, 1.0 - 2.0 * mc)))
     return out
 

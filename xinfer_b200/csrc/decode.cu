@@ -33,6 +33,10 @@ struct XbModel {
   int num_sms = 0;
 };
 
+#ifndef XB_MIN_SPLIT_POSITIONS
+#define XB_MIN_SPLIT_POSITIONS 4
+#endif
+
 namespace xb {
 
 struct WsLayout {
@@ -325,9 +329,10 @@ int xb_decode_step(const XbModel *model, const XbStepArgs *args, void *workspace
   p.dk_scale = (float)(1.0 / std::sqrt((double)p.DK));
   p.att_scale = (float)(1.0 / std::sqrt((double)g.head_dim));
   p.pstride = Lb.pstride;
-  // split-KV: enough (row, kv head, split) items to cover every SM, >= 4 positions per split
+  // split-KV: enough (row, kv head, split) items to cover every SM, but at least
+  // XB_MIN_SPLIT_POSITIONS positions per split (fewer partials for the combine to merge)
   int splits = std::max(1, ncta / std::max(1, active * g.num_kv_heads));
-  splits = std::min(splits, std::max(1, (max_kv + 3) / 4));
+  splits = std::min(splits, std::max(1, (max_kv + XB_MIN_SPLIT_POSITIONS - 1) / XB_MIN_SPLIT_POSITIONS));
   splits = std::min(splits, std::min(Lb.max_splits, 160));
   p.splits = splits;
   p.ncta = ncta;

@@ -1613,12 +1613,17 @@ template <int NB> struct Consumer {
         const unsigned *src = isk ? x + koff + kvh * D : x + hq * qrow;
         const bf16 *nw = (const bf16 *)(isk ? w.k_norm : w.q_norm);
         float v[8], ss = 0.f;
+        uint4 q4[2];
+        auto qaddr = [&](int i) { return src + lane * EPL + 4 * i; };
+        auto qwant = [&](int i) { return 4 * i < EPL; };
 #pragma unroll
-        for (int e4 = 0; e4 < 8; e4 += 4)
-          if (e4 < EPL) {
-            const uint4 q4 = poll4(src + lane * EPL + e4, tg);
-            v[e4] = bf_lo(q4.x); v[e4 + 1] = bf_lo(q4.y); v[e4 + 2] = bf_lo(q4.z); v[e4 + 3] = bf_lo(q4.w);
-          }
+        for (int i = 0; i < 2; ++i) q4[i] = qwant(i) ? ldcg_u4(qaddr(i)) : make_uint4(0, 0, 0, 0);
+        settle(q4, qaddr, qwant, [&](const uint4 &w4) { return tag4_ok(w4, tg); });
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          v[4 * i] = bf_lo(q4[i].x); v[4 * i + 1] = bf_lo(q4[i].y);
+          v[4 * i + 2] = bf_lo(q4[i].z); v[4 * i + 3] = bf_lo(q4[i].w);
+        }
 #pragma unroll
         for (int e = 0; e < 8; ++e)
           if (e < EPL) ss = fmaf(v[e], v[e], ss);
@@ -1650,14 +1655,19 @@ template <int NB> struct Consumer {
         for (int e = 0; e < 8; ++e)
           if (e < EPL) dst[lane * EPL + e] = v[e];
       } else if (warp == G + 1) {
+        uint4 v4[2];
+        auto vaddr = [&](int i) { return x + voff + kvh * D + lane * EPL + 4 * i; };
+        auto vwant = [&](int i) { return 4 * i < EPL; };
 #pragma unroll
-        for (int e4 = 0; e4 < 8; e4 += 4)
-          if (e4 < EPL) {
-            const uint4 q4 = poll4(x + voff + kvh * D + lane * EPL + e4, tg);
-            vn[lane * EPL + e4] = bf_lo(q4.x);
-            vn[lane * EPL + e4 + 1] = bf_lo(q4.y);
-            vn[lane * EPL + e4 + 2] = bf_lo(q4.z);
-            vn[lane * EPL + e4 + 3] = bf_lo(q4.w);
+        for (int i = 0; i < 2; ++i) v4[i] = vwant(i) ? ldcg_u4(vaddr(i)) : make_uint4(0, 0, 0, 0);
+        settle(v4, vaddr, vwant, [&](const uint4 &w4) { return tag4_ok(w4, tg); });
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+          if (4 * i < EPL) {
+            vn[lane * EPL + 4 * i] = bf_lo(v4[i].x);
+            vn[lane * EPL + 4 * i + 1] = bf_lo(v4[i].y);
+            vn[lane * EPL + 4 * i + 2] = bf_lo(v4[i].z);
+            vn[lane * EPL + 4 * i + 3] = bf_lo(v4[i].w);
           }
       }
       csync();
