@@ -45,6 +45,9 @@ def floor_bounds(per_step, window=16):
     return out
 
 
+_MODELS = {}
+
+
 def model(name, capacity, device, jitter=0.1, seed=0):
     key = (name, capacity, jitter, seed)
     if key not in _MODELS:
