@@ -149,6 +149,35 @@ int xb_workspace_check(void *workspace, void *stream, int32_t *device_error);
 int xb_decode_step_static(const XbGeometry *geometry, const XbModelWeights *weights,
                           const XbStepArgs *args, void *stream, int32_t *device_error);
 
+/* Prefix attention of up to 512 queries per row over a KV cache: the computation behind the
+ * reference's xinfer::flash_attention and xinfer::batched_flash_attention operators
+ * (compiler/common/kernels/attention.cpp:14-79 batched, :82-124 single extent), which call ATen's
+ * FlashAttention-2 there. Query t < count_b of row b sits at position length_b - count_b + t and
+ * attends to KV slots 0..length_b - count_b + t (lower-right causal); query head h reads KV head
+ * h / (q_heads / kv_heads); queries t >= count_b get zeros. bf16 tensors with unit feature stride:
+ *   q   [batch, q_heads, q_tokens, head_dim]   strides[0..2] = batch, head, token strides
+ *   k,v [batch, kv_heads, capacity, head_dim]  strides[3..5] (k) and [6..8] (v)
+ *   out [batch, q_heads, q_tokens, head_dim]   contiguous, fully written
+ * Per-row extents come from cu_offsets (device int32 [2, batch + 1]: cumulative query counts, then
+ * cumulative KV lengths, as batched_attention_metadata builds them, compiler/common/attention.py
+ * :27-40) or, when cu_offsets is NULL, are the same (count, length) for every row. Strides must be
+ * multiples of 8 elements and tensors 16-byte aligned. `blocks` is the one-block-per-row page
+ * table of the batched operator (attention.cpp:58-63). Errors: XB_ERR_INVALID with the
+ * reference's messages ("Query heads must be a positive multiple of KV heads", "Flash head
+ * dimension must be a multiple of 8 in 8..256", "Invalid valid-prefix length"). */
+typedef struct XbAttentionArgs {
+  const void *q, *k, *v;
+  void *out;
+  long long strides[9];
+  int32_t batch, q_heads, kv_heads, head_dim, q_tokens, capacity;
+  const int32_t *cu_offsets;
+  int32_t count, length;
+  float scale;
+  const int32_t *blocks;     /* device int32: row b reads cache row blocks[b * blocks_stride], or NULL: b */
+  long long blocks_stride;
+} XbAttentionArgs;
+int xb_prefix_attention(const XbAttentionArgs *args, void *stream);
+
 /* Host-only helper: the HF default RoPE inverse frequencies 1 / theta^(2i / rotary_dim) in fp32
  * (transformers Qwen3_5TextRotaryEmbedding.compute_default_rope_parameters, as loaded by
  * compiler/qwen35/model.py:41 and compiler/qwen3/model.py:16-26). */

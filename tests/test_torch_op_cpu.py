@@ -49,6 +49,22 @@ def test_schemas(ops):
                           f"float[] params) -> {ret}")
 
 
+def test_attention_schemas(ops):
+    """The reference's schemas and tags (compiler/common/kernels/attention.cpp:128-135)."""
+    assert str(ops.batched_flash_attention.default._schema) == (
+        "xinfer::batched_flash_attention(Tensor q, Tensor k, Tensor v, Tensor offsets, "
+        "Tensor cuda_offsets, Tensor blocks, float scale) -> Tensor")
+    assert str(ops.flash_attention.default._schema) == (
+        "xinfer::flash_attention(Tensor q, Tensor k, Tensor v, Tensor kv_extent, float scale) -> Tensor")
+    for op in (ops.batched_flash_attention.default, ops.flash_attention.default):
+        assert torch.Tag.flexible_layout in op.tags
+    with FakeTensorMode():
+        q = torch.empty(2, 16, 5, 128, dtype=torch.bfloat16, device="cuda")
+        k = torch.empty(2, 8, 64, 128, dtype=torch.bfloat16, device="cuda")
+        out = ops.flash_attention(q, k, k, torch.empty(9, dtype=torch.uint8), 128 ** -0.5)
+        assert out.shape == q.shape and out.is_contiguous()
+
+
 def _fake_args(g, batch, capacity):
     geometry, params = torch_ops.geometry_args(g, capacity)
     ids = torch.zeros((batch, 1), dtype=torch.int64, device="cuda")

@@ -23,6 +23,7 @@ EXPORTED = (
     "xb_model_create", "xb_model_destroy", "xb_decode_workspace_bytes", "xb_workspace_init",
     "xb_decode_step", "xb_workspace_check", "xb_rope_inv_freq", "xb_last_error",
     "xb_abi_version", "xb_decode_step_static", "xb_debug_trace", "xb_debug_fault",
+    "xb_prefix_attention",
 )
 TRACE_STAGES = 512
 TRACE_STRIDE = 3 * TRACE_STAGES + 8
@@ -93,6 +94,16 @@ class NativeError(RuntimeError):
 _lib = None
 
 
+class XbAttentionArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", vp), ("k", vp), ("v", vp), ("out", vp), ("strides", ctypes.c_longlong * 9),
+        ("batch", ctypes.c_int32), ("q_heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32), ("q_tokens", ctypes.c_int32), ("capacity", ctypes.c_int32),
+        ("cu_offsets", vp), ("count", ctypes.c_int32), ("length", ctypes.c_int32),
+        ("scale", ctypes.c_float), ("blocks", vp), ("blocks_stride", ctypes.c_longlong),
+    ]
+
+
 def library_path():
     override = os.environ.get("XINFER_B200_LIBRARY")
     return Path(override).resolve() if override else LIBRARY_PATH
@@ -120,6 +131,7 @@ def load():
         "xb_decode_step": (i32, [vp, ctypes.POINTER(XbStepArgs), vp, sz, vp]),
         "xb_workspace_check": (i32, [vp, vp, ctypes.POINTER(i32)]),
         "xb_rope_inv_freq": (i32, [ctypes.c_float, i32, ctypes.POINTER(ctypes.c_float)]),
+        "xb_prefix_attention": (i32, [ctypes.POINTER(XbAttentionArgs), vp]),
         "xb_decode_step_static": (i32, [ctypes.POINTER(XbGeometry), ctypes.POINTER(XbModelWeights),
                                         ctypes.POINTER(XbStepArgs), vp, ctypes.POINTER(i32)]),
         "xb_debug_trace": (i32, [vp, sz]),

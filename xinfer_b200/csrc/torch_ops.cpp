@@ -32,6 +32,7 @@
 #include <torch/csrc/inductor/aoti_torch/utils.h>
 #include <torch/library.h>
 
+#include <cmath>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -242,9 +243,119 @@ at::Tensor qwen3_decode_step(const at::Tensor &input_ids, const at::Tensor &cach
                      weights, geometry, params)[0];
 }
 
+// ---- xinfer_attention_ops: the reference's attention operators on libxinfer_b200's kernel ----
+// Same schemas, checks and contract as compiler/common/kernels/attention.cpp:14-140: fresh
+// contiguous outputs that never alias the inputs, inputs never modified, inference only.
+
+// A view the kernel can read directly: unit feature stride, 8-element strides, 16-byte aligned.
+static at::Tensor kernel_view(const at::Tensor &t) {
+  bool ok = t.stride(3) == 1 && (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0;
+  for (int i = 0; i < 3; ++i) ok = ok && t.stride(i) % 8 == 0;
+  return ok ? t : t.contiguous();
+}
+
+static at::Tensor run_attention(const at::Tensor &q, const at::Tensor &k, const at::Tensor &v,
+                                const int32_t *cu, int32_t count, int32_t length,
+                                const at::Tensor *blocks, double scale) {
+  c10::cuda::CUDAGuard guard(q.device());
+  const at::Tensor query = kernel_view(q), key = kernel_view(k), value = kernel_view(v);
+  at::Tensor out = at::empty(q.sizes(), q.options().memory_format(at::MemoryFormat::Contiguous));
+  XbAttentionArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.q = query.data_ptr();
+  a.k = key.data_ptr();
+  a.v = value.data_ptr();
+  a.out = out.data_ptr();
+  const at::Tensor *t[3] = {&query, &key, &value};
+  for (int i = 0; i < 3; ++i)
+    for (int j = 0; j < 3; ++j) a.strides[3 * i + j] = t[i]->stride(j);
+  a.batch = (int32_t)q.size(0);
+  a.q_heads = (int32_t)q.size(1);
+  a.kv_heads = (int32_t)k.size(1);
+  a.head_dim = (int32_t)q.size(3);
+  a.q_tokens = (int32_t)q.size(2);
+  a.capacity = (int32_t)k.size(2);
+  a.cu_offsets = cu;
+  a.count = count;
+  a.length = length;
+  a.scale = (float)scale;
+  if (blocks) {
+    a.blocks = blocks->data_ptr<int32_t>();
+    a.blocks_stride = blocks->stride(0);
+  }
+  check_rc(xb_prefix_attention(&a, at::cuda::getCurrentCUDAStream(q.device().index()).stream()),
+           "xb_prefix_attention");
+  return out;
+}
+
+static void check_qkv_common(const at::Tensor &q, const at::Tensor &k, const at::Tensor &v, double scale) {
+  TORCH_CHECK(q.size(1) > 0 && k.size(1) > 0 && q.size(1) % k.size(1) == 0,
+              "Query heads must be a positive multiple of KV heads");
+  TORCH_CHECK(q.size(3) >= 8 && q.size(3) <= 256 && q.size(3) % 8 == 0,
+              "Flash head dimension must be a multiple of 8 in 8..256");
+  TORCH_CHECK(std::isfinite(scale) && scale > 0, "Attention scale must be finite and positive");
+  TORCH_CHECK(!q.requires_grad() && !k.requires_grad() && !v.requires_grad(),
+              "xinfer attention supports inference only");
+}
+
+at::Tensor flash_attention(const at::Tensor &q, const at::Tensor &k, const at::Tensor &v,
+                           const at::Tensor &extent, double scale) {
+  TORCH_CHECK(q.is_cuda() && k.device() == q.device() && v.device() == q.device(),
+              "xinfer attention requires Q/K/V on the same CUDA device");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 &&
+                  v.scalar_type() == at::kBFloat16,
+              "xinfer attention requires BF16");
+  TORCH_CHECK(q.dim() == 4 && q.size(0) > 0 && q.size(2) >= 1 && q.size(2) <= 512, "Unsupported Q shape");
+  TORCH_CHECK(k.dim() == 4 && v.dim() == 4 && k.size(0) == q.size(0) && k.size(2) > 0 &&
+                  k.size(3) == q.size(3) && v.sizes() == k.sizes(),
+              "Expected matching full-capacity K/V inputs [batch,kv_heads,capacity,head_dim]");
+  check_qkv_common(q, k, v, scale);
+  TORCH_CHECK(extent.device().is_cpu() && extent.scalar_type() == at::kByte && extent.dim() == 1,
+              "Expected a CPU uint8 extent vector");
+  const int64_t length = extent.size(0) - 1;  // metadata only; the extent's data is never read
+  TORCH_CHECK(length >= q.size(2) && length <= k.size(2), "Invalid valid-prefix length");
+  return run_attention(q, k, v, nullptr, (int32_t)q.size(2), (int32_t)length, nullptr, scale);
+}
+
+at::Tensor batched_flash_attention(const at::Tensor &q, const at::Tensor &k, const at::Tensor &v,
+                                   const at::Tensor &offsets, const at::Tensor &cuda_offsets,
+                                   const at::Tensor &blocks, double scale) {
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.sizes() == k.sizes() && k.size(0) == q.size(0) &&
+                  k.size(3) == q.size(3),
+              "Invalid Q/K/V shapes");
+  TORCH_CHECK(q.is_cuda() && k.device() == q.device() && v.device() == q.device() &&
+                  q.scalar_type() == at::kBFloat16 && k.scalar_type() == q.scalar_type() &&
+                  v.scalar_type() == q.scalar_type(),
+              "Expected colocated CUDA BF16 Q/K/V");
+  TORCH_CHECK(q.size(2) >= 1 && q.size(2) <= 512, "Unsupported Q shape");
+  check_qkv_common(q, k, v, scale);
+  const int64_t batch = q.size(0);
+  TORCH_CHECK(offsets.device().is_cpu() && offsets.scalar_type() == at::kInt && offsets.is_contiguous() &&
+                  offsets.sizes() == at::IntArrayRef({2, batch + 1}),
+              "Expected CPU int32 cumulative query/KV lengths [2,B+1]");
+  TORCH_CHECK(cuda_offsets.device() == q.device() && cuda_offsets.scalar_type() == at::kInt &&
+                  cuda_offsets.sizes() == offsets.sizes() && cuda_offsets.is_contiguous() &&
+                  blocks.device() == q.device() && blocks.scalar_type() == at::kInt &&
+                  blocks.sizes() == at::IntArrayRef({batch, 1}),
+              "Invalid CUDA attention metadata");
+  const int32_t *cuq = offsets.const_data_ptr<int32_t>(), *cuk = cuq + batch + 1;
+  TORCH_CHECK(cuq[0] == 0 && cuk[0] == 0, "Cumulative lengths must start at zero");
+  for (int64_t row = 0; row < batch; ++row) {
+    const int64_t count = cuq[row + 1] - cuq[row], length = cuk[row + 1] - cuk[row];
+    TORCH_CHECK(count >= 0 && count <= q.size(2) && length >= count && length >= 1 && length <= k.size(2),
+                "Invalid query/KV lengths");
+  }
+  return run_attention(q, k, v, cuda_offsets.data_ptr<int32_t>(), 0, 0, &blocks, scale);
+}
+
 } // namespace xinfer_b200
 
 TORCH_LIBRARY_FRAGMENT(xinfer, m) {
+  m.def("batched_flash_attention(Tensor q, Tensor k, Tensor v, Tensor offsets, "
+        "Tensor cuda_offsets, Tensor blocks, float scale) -> Tensor",
+        {at::Tag::flexible_layout});
+  m.def("flash_attention(Tensor q, Tensor k, Tensor v, Tensor kv_extent, float scale) -> Tensor",
+        {at::Tag::flexible_layout});
   m.def("qwen35_decode_step(Tensor input_ids, Tensor cache_position, Tensor(a!)[] state, "
         "Tensor kv_lengths, Tensor query_lengths, Tensor[] weights, int[] geometry, "
         "float[] params) -> Tensor[]");
@@ -256,6 +367,8 @@ TORCH_LIBRARY_FRAGMENT(xinfer, m) {
 TORCH_LIBRARY_IMPL(xinfer, CUDA, m) {
   m.impl("qwen35_decode_step", TORCH_FN(xinfer_b200::qwen35_decode_step));
   m.impl("qwen3_decode_step", TORCH_FN(xinfer_b200::qwen3_decode_step));
+  m.impl("batched_flash_attention", TORCH_FN(xinfer_b200::batched_flash_attention));
+  m.impl("flash_attention", TORCH_FN(xinfer_b200::flash_attention));
 }
 
 // AOTInductor C shims (the pattern of compiler/common/kernels/attention_shim.cpp:5-32): borrowed
@@ -294,6 +407,33 @@ extern "C" AOTI_TORCH_EXPORT AOTITorchError aoti_torch_cuda_qwen3_decode_step(
         ai::resolve_tensor_dispatch_flags(kv_lengths), ai::resolve_tensor_dispatch_flags(query_lengths),
         ai::resolve_tensor_list_dispatch_flags(weights, weights_len_),
         at::IntArrayRef(geometry, (size_t)geometry_len_), at::ArrayRef<double>(params, (size_t)params_len_));
+    *output = ai::new_tensor_handle(std::move(result));
+  });
+}
+
+// The attention operators' shims, with the reference's signatures
+// (compiler/common/attention.py:10-16).
+extern "C" AOTI_TORCH_EXPORT AOTITorchError aoti_torch_cuda_batched_flash_attention(
+    AtenTensorHandle q, AtenTensorHandle k, AtenTensorHandle v, AtenTensorHandle offsets,
+    AtenTensorHandle cuda_offsets, AtenTensorHandle blocks, double scale, AtenTensorHandle *output) {
+  AOTI_TORCH_CONVERT_EXCEPTION_TO_ERROR_CODE({
+    namespace ai = torch::aot_inductor;
+    auto result = xinfer_b200::batched_flash_attention(
+        ai::resolve_tensor_dispatch_flags(q), ai::resolve_tensor_dispatch_flags(k),
+        ai::resolve_tensor_dispatch_flags(v), ai::resolve_tensor_dispatch_flags(offsets),
+        ai::resolve_tensor_dispatch_flags(cuda_offsets), ai::resolve_tensor_dispatch_flags(blocks), scale);
+    *output = ai::new_tensor_handle(std::move(result));
+  });
+}
+
+extern "C" AOTI_TORCH_EXPORT AOTITorchError aoti_torch_cuda_flash_attention(
+    AtenTensorHandle q, AtenTensorHandle k, AtenTensorHandle v, AtenTensorHandle extent, double scale,
+    AtenTensorHandle *output) {
+  AOTI_TORCH_CONVERT_EXCEPTION_TO_ERROR_CODE({
+    namespace ai = torch::aot_inductor;
+    auto result = xinfer_b200::flash_attention(
+        ai::resolve_tensor_dispatch_flags(q), ai::resolve_tensor_dispatch_flags(k),
+        ai::resolve_tensor_dispatch_flags(v), ai::resolve_tensor_dispatch_flags(extent), scale);
     *output = ai::new_tensor_handle(std::move(result));
   });
 }

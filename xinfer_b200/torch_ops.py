@@ -1,6 +1,9 @@
-"""Torch custom operators of the decode step: xinfer::qwen35_decode_step and
-xinfer::qwen3_decode_step (xinfer_b200/csrc/torch_ops.cpp, built into
-xinfer_b200/libxinfer_b200_ops.so), with the fake kernels that torch.export / AOTInductor trace.
+"""Torch custom operators (xinfer_b200/csrc/torch_ops.cpp, built into
+xinfer_b200/libxinfer_b200_ops.so) with the fake kernels that torch.export / AOTInductor trace:
+the decode step, xinfer::qwen35_decode_step and xinfer::qwen3_decode_step, and the reference's
+attention operators xinfer::flash_attention and xinfer::batched_flash_attention
+(compiler/common/kernels/attention.cpp:128-140) backed by this library's sm_100a attention kernel
+instead of ATen's FlashAttention-2, so the library can stand in for libxinfer_attention_ops.so.
 
 The operators keep ModelStep.forward's T == 1 contract (compiler/qwen35/model.py:162-183,
 compiler/qwen3/model.py:70-95) and carry the model as arguments, the way an exported graph
@@ -99,6 +102,29 @@ def load(library=None):
         torch._check(geometry[0] == FAMILY["qwen3"])
         _check_inputs(input_ids, cache_position, state, kv_lengths, query_lengths, geometry)
         return _fake_outputs(input_ids, state, geometry)[0]
+
+    @torch.library.register_fake("xinfer::flash_attention")
+    def fake_attention(q, k, v, kv_extent, scale):
+        # as the reference's registration (compiler/common/attention.py:63-82): output
+        # metadata depends on Q only; the valid-prefix length is checked natively
+        torch._check(q.dim() == 4 and k.dim() == 4 and v.dim() == 4)
+        torch._check(q.shape[0] > 0 and q.shape[1] > 0 and k.shape[1] > 0)
+        torch._check(q.shape[1] % k.shape[1] == 0)
+        torch._check(q.shape[3] >= 8 and q.shape[3] <= 256 and q.shape[3] % 8 == 0)
+        torch._check(q.shape[2] >= 1 and q.shape[2] <= 512 and k.shape[2] > 0)
+        torch._check(k.shape == (q.shape[0], k.shape[1], k.shape[2], q.shape[3]) and v.shape == k.shape)
+        torch._check(q.dtype == k.dtype == v.dtype == torch.bfloat16)
+        torch._check(q.device.type == "cuda" and k.device == q.device and v.device == q.device)
+        torch._check(kv_extent.device.type == "cpu" and kv_extent.dtype == torch.uint8 and kv_extent.dim() == 1)
+        return q.new_empty(q.shape)
+
+    @torch.library.register_fake("xinfer::batched_flash_attention")
+    def fake_batched(q, k, v, offsets, cuda_offsets, blocks, scale):
+        torch._check(offsets.device.type == "cpu" and offsets.dtype == torch.int32)
+        torch._check(offsets.shape == (2, q.shape[0] + 1))
+        torch._check(cuda_offsets.shape == offsets.shape and cuda_offsets.device == q.device)
+        torch._check(blocks.shape == (q.shape[0], 1) and blocks.device == q.device)
+        return fake_attention(q, k, v, torch.empty(2, dtype=torch.uint8), scale)
 
     _loaded = True
 
