@@ -178,6 +178,33 @@ typedef struct XbAttentionArgs {
 } XbAttentionArgs;
 int xb_prefix_attention(const XbAttentionArgs *args, void *stream);
 
+/* Prefill of one row: ModelStep.forward with T > 1 tokens (compiler/qwen35/model.py:162-183,
+ * compiler/qwen3/model.py:70-95, exported as prefill.pt2 by compiler/qwen35/export.py:43-57, run by
+ * runtime/common/runner.h:30-78 for prompts). T tokens (1..512) at cache positions
+ * start_position .. start_position + T - 1 of state row 0: K/V appended in place, the DeltaNet
+ * conv window and recurrent state read from *_in and written to *_out (equal pointers update in
+ * place), the logits of the last token written to `logits` (bf16 [vocab]) and its argmax to
+ * `next_token` (or skipped when NULL). The projections run on the tensor cores (xb_gemm_bf16);
+ * the DeltaNet recurrence is scanned over the tokens. The workspace (xb_prefill_workspace_bytes)
+ * starts with the decode workspace's control words: token ids out of range are reported by
+ * xb_workspace_check. Calls that overlap on the GPU must not share a workspace. */
+typedef struct XbPrefillArgs {
+  int32_t tokens;
+  const int64_t *input_ids;           /* device int64 [T] */
+  int64_t start_position;
+  XbLayerState layers[XB_MAX_LAYERS]; /* row 0 of every state tensor */
+  void *logits;                       /* device bf16 [vocab] */
+  int64_t *next_token;                /* device int64 [1], or NULL */
+} XbPrefillArgs;
+int xb_prefill_workspace_bytes(const XbModel *model, int32_t max_tokens, size_t *bytes);
+int xb_prefill_step(const XbModel *model, const XbPrefillArgs *args, void *workspace,
+                    size_t workspace_bytes, void *stream);
+
+/* out[m, n] = x[m, k] . w[n, k]^T in bf16 with fp32 accumulation and one rounding: the bf16
+ * nn.Linear of the reference's prefill graph (cuBLAS through Inductor there), on the sm_100a
+ * tensor cores. n and k multiples of 8, all pointers 16-byte aligned, row-major and packed. */
+int xb_gemm_bf16(int32_t m, int32_t n, int32_t k, const void *x, const void *w, void *out, void *stream);
+
 /* Host-only helper: the HF default RoPE inverse frequencies 1 / theta^(2i / rotary_dim) in fp32
  * (transformers Qwen3_5TextRotaryEmbedding.compute_default_rope_parameters, as loaded by
  * compiler/qwen35/model.py:41 and compiler/qwen3/model.py:16-26). */

@@ -23,7 +23,7 @@ EXPORTED = (
     "xb_model_create", "xb_model_destroy", "xb_decode_workspace_bytes", "xb_workspace_init",
     "xb_decode_step", "xb_workspace_check", "xb_rope_inv_freq", "xb_last_error",
     "xb_abi_version", "xb_decode_step_static", "xb_debug_trace", "xb_debug_fault",
-    "xb_prefix_attention",
+    "xb_prefix_attention", "xb_prefill_workspace_bytes", "xb_prefill_step", "xb_gemm_bf16",
 )
 TRACE_STAGES = 512
 TRACE_STRIDE = 3 * TRACE_STAGES + 8
@@ -104,6 +104,13 @@ class XbAttentionArgs(ctypes.Structure):
     ]
 
 
+class XbPrefillArgs(ctypes.Structure):
+    _fields_ = [
+        ("tokens", ctypes.c_int32), ("input_ids", vp), ("start_position", ctypes.c_int64),
+        ("layers", XbLayerState * MAX_LAYERS), ("logits", vp), ("next_token", vp),
+    ]
+
+
 def library_path():
     override = os.environ.get("XINFER_B200_LIBRARY")
     return Path(override).resolve() if override else LIBRARY_PATH
@@ -132,6 +139,9 @@ def load():
         "xb_workspace_check": (i32, [vp, vp, ctypes.POINTER(i32)]),
         "xb_rope_inv_freq": (i32, [ctypes.c_float, i32, ctypes.POINTER(ctypes.c_float)]),
         "xb_prefix_attention": (i32, [ctypes.POINTER(XbAttentionArgs), vp]),
+        "xb_prefill_workspace_bytes": (i32, [vp, i32, ctypes.POINTER(sz)]),
+        "xb_prefill_step": (i32, [vp, ctypes.POINTER(XbPrefillArgs), vp, sz, vp]),
+        "xb_gemm_bf16": (i32, [i32, i32, i32, vp, vp, vp, vp]),
         "xb_decode_step_static": (i32, [ctypes.POINTER(XbGeometry), ctypes.POINTER(XbModelWeights),
                                         ctypes.POINTER(XbStepArgs), vp, ctypes.POINTER(i32)]),
         "xb_debug_trace": (i32, [vp, sz]),

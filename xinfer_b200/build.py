@@ -25,6 +25,17 @@ OPS_SRC = CSRC / "torch_ops.cpp"
 OPS_OUT = PKG / "libxinfer_b200_ops.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def cutlass_includes():
+    """CUTLASS / CuTe header trees (4.x, with the SM100 collectives) vendored in this image."""
+    import flashinfer  # the header tree ships as package data
+
+    root = Path(flashinfer.__file__).resolve().parent / "data" / "cutlass"
+    inc = [root / "include", root / "tools" / "util" / "include"]
+    if not all((p / "cutlass").is_dir() for p in inc):
+        raise RuntimeError(f"CUTLASS headers not found under {root}")
+    return [f"-I{p}" for p in inc]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
          "--expt-relaxed-constexpr", "-Xptxas", "-v"]
 
@@ -84,7 +95,7 @@ def up_to_date():
 def build(force=False, verbose=False):
     if not force and up_to_date():
         return OUT
-    cmd = [nvcc(), *ARCH, *FLAGS, f"-I{INCLUDE}", f"-I{CSRC}", "-o", str(OUT) + ".tmp",
+    cmd = [nvcc(), *ARCH, *FLAGS, f"-I{INCLUDE}", f"-I{CSRC}", *cutlass_includes(), "-o", str(OUT) + ".tmp",
            *map(str, sources())]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     log = proc.stdout + proc.stderr

@@ -23,11 +23,8 @@
 
 #include <string>
 
-#include "xinfer_b200.h"
+#include "xb_host.h"
 
-namespace xb {
-int fail(int code, const std::string &msg);
-}
 
 namespace xbattn {
 

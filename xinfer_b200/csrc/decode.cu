@@ -2,6 +2,7 @@
 // The kernels of batch rows 1 and 2 are compiled here; those of 4 and 8 in decode_tc.cu.
 
 #include "decode_kernel.cuh"
+#include "xb_host.h"
 
 namespace xb {
 
@@ -23,15 +24,6 @@ int fail(int code, const std::string &msg) {
   } while (0)
 
 } // namespace xb
-
-struct XbModel {
-  XbGeometry g;
-  XbModelWeights w;
-  XbLayerWeights *d_layers = nullptr;  // device table
-  float *d_inv_freq = nullptr;
-  int device = 0;
-  int num_sms = 0;
-};
 
 #ifndef XB_MIN_SPLIT_POSITIONS
 #define XB_MIN_SPLIT_POSITIONS 4

@@ -105,6 +105,7 @@ class Engine:
         self._args = nat.XbStepArgs()
         self._ws_ptr, self._ws_bytes = self.workspace.data_ptr(), self.workspace.numel()
         self._bound_in = self._bound_out = None
+        self._prefill_ws = None
 
     def close(self):
         if getattr(self, "handle", None):
@@ -182,6 +183,50 @@ class Engine:
                 ls.k_cache, ls.v_cache = s0.data_ptr(), s1.data_ptr()
                 ls.conv_in = ls.rec_in = ls.conv_out = ls.rec_out = None
         self._bound_in, self._bound_out = state_in, state_out
+
+    # -- prefill ----------------------------------------------------------------------------
+    def prefill(self, input_ids, start_position, state_in, state_out, logits, next_token=None,
+                stream=None):
+        """ModelStep.forward with T > 1 for one row (compiler/qwen35/model.py:162-183):
+        input_ids CUDA int64 [T] (1..512 tokens) at cache positions start_position..+T-1 of state
+        row 0; KV appended in place, DeltaNet state read from state_in and written to state_out
+        (the same list updates in place); logits of the last token into `logits` (bf16 [vocab]),
+        its argmax into `next_token` (int64 [1]) when given."""
+        T = int(input_ids.numel())
+        if not 1 <= T <= 512:
+            raise ValueError("prefill takes 1..512 tokens")
+        if input_ids.dtype != torch.int64 or input_ids.device != self.device or not input_ids.is_contiguous():
+            raise ValueError("input_ids must be a contiguous CUDA int64 tensor")
+        if self._prefill_ws is None:
+            nbytes = ctypes.c_size_t()
+            nat.check(self.lib.xb_prefill_workspace_bytes(self.handle, 512, ctypes.byref(nbytes)))
+            self._prefill_ws = torch.zeros(nbytes.value, dtype=torch.uint8, device=self.device)
+        a = nat.XbPrefillArgs()
+        a.tokens = T
+        a.input_ids = input_ids.data_ptr()
+        a.start_position = int(start_position)
+        for i in range(self.g.num_layers):
+            ls = a.layers[i]
+            s0, s1 = state_in[2 * i], state_in[2 * i + 1]
+            if self.g.is_delta(i):
+                o0, o1 = state_out[2 * i], state_out[2 * i + 1]
+                ls.conv_in, ls.rec_in = s0.data_ptr(), s1.data_ptr()
+                ls.conv_out, ls.rec_out = o0.data_ptr(), o1.data_ptr()
+            else:
+                ls.k_cache, ls.v_cache = s0.data_ptr(), s1.data_ptr()
+        a.logits = logits.data_ptr()
+        a.next_token = next_token.data_ptr() if next_token is not None else None
+        st = stream if stream is not None else torch.cuda.current_stream(self.device)
+        nat.check(self.lib.xb_prefill_step(self.handle, ctypes.byref(a), self._prefill_ws.data_ptr(),
+                                           self._prefill_ws.numel(), ctypes.c_void_p(st.cuda_stream)))
+
+    def check_prefill_error(self, stream=None):
+        if self._prefill_ws is None:
+            return
+        st = stream if stream is not None else torch.cuda.current_stream(self.device)
+        err = ctypes.c_int32()
+        nat.check(self.lib.xb_workspace_check(self._prefill_ws.data_ptr(), ctypes.c_void_p(st.cuda_stream),
+                                              ctypes.byref(err)))
 
     def check_device_error(self, stream=None):
         st = stream if stream is not None else torch.cuda.current_stream(self.device)
@@ -280,13 +325,24 @@ class Runner:
         return self.step_batch([list(tokens)])
 
     def prefill(self, prompt):
-        """Feeds the prompt one token per call through the decode kernel (row 0)."""
+        """Row 0's prompt through the prefill path in chunks of up to 512 tokens (the reference
+        runner's prefill.pt2 calls, runtime/common/runner.h:30-78); the last token's logits and
+        greedy token land in logits[0] / next_tokens[0]."""
         if len(prompt) > self.engine.capacity - self.positions[0]:
             raise ValueError("Context capacity exceeded")
-        logits = None
+        if self.positions[0] + len(prompt) == 0:
+            raise ValueError("Each row must start with tokens")
         for t in prompt:
-            logits = self.step([t])
-        return logits
+            if not 0 <= t < self.g.vocab:
+                raise ValueError("token id out of range")
+        dev = self.engine.device
+        for c0 in range(0, len(prompt), 512):
+            chunk = torch.tensor(prompt[c0:c0 + 512], dtype=torch.int64).to(dev)
+            self.engine.prefill(chunk, self.positions[0], self.state, self.state, self.logits[0],
+                                self.next_tokens[:1])
+            self.positions[0] += chunk.numel()
+        self.decode_calls += 1
+        return self.logits[:1]
 
     def next_token(self, row=0):
         self._tok_host.copy_(self.next_tokens)
