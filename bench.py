@@ -57,6 +57,9 @@ def parse():
                     help="budget of the secondary CPU-oracle figure")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--trace", help="save a per-CTA stage trace of one extra step to this file")
+    ap.add_argument("--measure", choices=("decode", "prefill"), default="decode",
+                    help="prefill: time the prompt's 512-token prefill chunks instead (tokens/s and "
+                         "tensor-pipe utilisation of the projections)")
     return ap.parse_args()
 
 
@@ -106,6 +109,96 @@ def algorithmic_bytes(g, contexts):
         total += n_delta * 2 * (rec + conv)
         total += n_attn * kv_token * (context + 1)
     return total
+
+
+def prefill_flops(g, chunks):
+    """Algorithmic FLOPs of prefilling chunks [(start, T), ...]: every projection of every layer
+    (2 K N per token; the packed in_proj, q|k|v, o/out_proj, gate, up, down), the prefix attention
+    (4 D per visible key and query head: Q.K^T and P.V) and the DeltaNet scan (about 8 dk dv per
+    token and value head), and the lm_head of the last token only."""
+    H, I = g.hidden, g.intermediate
+    per_token = 0
+    attn = 0
+    for i in range(g.num_layers):
+        if g.is_delta(i):
+            hv = g.lin_value_heads * g.lin_head_dim
+            per_token += 2 * H * (g.conv_channels + hv + 2 * g.lin_value_heads) + 2 * hv * H
+            per_token += 8 * g.lin_value_heads * g.lin_head_dim * g.lin_head_dim
+        else:
+            per_token += 2 * H * (g.q_rows + 2 * g.num_kv_heads * g.head_dim) + 2 * g.num_q_heads * g.head_dim * H
+            attn += 1
+        per_token += 2 * H * 2 * I + 2 * I * H
+    total = 0
+    for start, T in chunks:
+        total += per_token * T
+        # keys visible to query t: start + t + 1
+        total += attn * 4 * g.head_dim * g.num_q_heads * (T * start + T * (T + 1) // 2)
+    return total + 2 * g.vocab * H
+
+
+def measure_prefill(args, dist, dev, world, rank):
+    """Prefill throughput of the prompt in 512-token chunks."""
+    from xinfer_b200 import configs, synthetic
+    from xinfer_b200.engine import Engine
+
+    g = configs.get(args.config)
+    weights = synthetic.make_state_dict(g, seed=0, device=dev)
+    eng = Engine(g, weights, capacity=args.capacity, device=dev)
+    prompt = synthetic.random_prompt(g, args.prompt, seed=1000 + rank)
+    ids = torch.tensor(prompt, dtype=torch.int64).to(dev)
+    state = [t.narrow(0, 0, 1) for t in eng.allocate_state()]
+    logits = torch.empty(g.vocab, dtype=torch.bfloat16, device=dev)
+    nxt = torch.empty(1, dtype=torch.int64, device=dev)
+    chunks = [(c, min(512, args.prompt - c)) for c in range(0, args.prompt, 512)]
+    stream = torch.cuda.current_stream(dev)
+
+    def run_prompt():
+        for start, T in chunks:
+            eng.prefill(ids[start:start + T], start, state, state, logits, nxt)
+
+    for _ in range(max(1, args.warmup)):
+        run_prompt()
+    eng.check_prefill_error()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, args.steps)
+    with Clocks(dev.index or 0) as clocks:
+        ev0.record(stream)
+        for _ in range(steps):
+            run_prompt()
+        ev1.record(stream)
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+    ms = max_over_ranks(ev0.elapsed_time(ev1), dist, dev)
+    eng.check_prefill_error()
+    tokens = steps * args.prompt
+    flops = steps * prefill_flops(g, chunks)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    achieved = flops / (ms / 1000.0) / 1e12
+    line = {
+        "metric": f"prefill tok/s ({args.config}, {args.prompt}-token prompt in 512-token chunks)",
+        "value": job_throughput(world, tokens, ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{args.config} prefill of a {args.prompt}-token random prompt per GPU in "
+                               f"{len(chunks)} chunks, {args.capacity}-slot capacity",
+                   "model": args.config, "global_batch": world, "seq_len": args.capacity},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_kind": "measured" if peaks else "fallback",
+                     "algorithmic_flops_per_step": flops / steps},
+        "clocks": clocks.summary(),
+    }
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
 
 
 def measured_peak():
@@ -202,14 +295,29 @@ def hf_eager_model(g):
 
     hf = configs.hf_config(g)
     hf._attn_implementation = "sdpa"
+    cpu_kernels = {}
     if g.family == configs.QWEN35:
         from transformers import Qwen3_5ForCausalLM as Model
+        from transformers.models.qwen3_5 import modeling_qwen3_5 as hf_module
         from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5TextRotaryEmbedding as Rotary
+        # the CPU build HF makes when the GPU-only fla / causal-conv1d kernels are absent: its
+        # torch Gated DeltaNet (chunked prefill, recurrent decode, conv update) and gated norm
+        cpu_kernels = {"FusedRMSNormGated": None, "chunk_gated_delta_rule": None,
+                       "fused_recurrent_gated_delta_rule": None, "causal_conv1d_fn": None,
+                       "causal_conv1d_update": None, "is_fast_path_available": False}
     else:
         from transformers import Qwen3ForCausalLM as Model
         from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding as Rotary
-    with torch.device("meta"):
-        model = Model(hf)
+        hf_module = None
+    saved = {name: getattr(hf_module, name) for name in cpu_kernels}
+    try:
+        for name, value in cpu_kernels.items():
+            setattr(hf_module, name, value)
+        with torch.device("meta"):
+            model = Model(hf)
+    finally:
+        for name, value in saved.items():
+            setattr(hf_module, name, value)
     model.load_state_dict(synthetic.make_state_dict(g, seed=0), strict=True, assign=True)
     model.lm_head.weight = model.model.embed_tokens.weight
     model.model.rotary_emb = Rotary(hf)
@@ -351,6 +459,8 @@ def main():
                                 device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.measure == "prefill":
+        return measure_prefill(args, dist, dev, world, rank)
 
     from xinfer_b200 import configs, synthetic
     from xinfer_b200.engine import Engine, Runner
@@ -379,6 +489,9 @@ def main():
 
     def prefill_rows():
         runner.reset()
+        if B == 1:  # the prompt through the prefill path (tensor-core GEMMs), 512 tokens per chunk
+            runner.prefill(prompts[0])
+            return
         for t in range(max(lengths)):
             runner.step_batch([[p[t]] if t < len(p) else [] for p in prompts])
 

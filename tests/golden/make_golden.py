@@ -136,9 +136,20 @@ def import_reference(path):
         )
 
     def fused(qkv, b, a, conv, state, weight, A_log, dt_bias, query_lengths=None):
-        # the arguments of the reference's `short` wrapper (recurrent.py:192-231)
+        # the reference's dispatch (recurrent.py:292-349): chunks longer than SHORT_THRESHOLD
+        # take its `long` path (prepare kernel + chunk-64 scan, recurrent.py:234-281), run as is
         batch, tokens = qkv.shape[:2]
-        assert tokens <= R.SHORT_THRESHOLD
+        if query_lengths is None:
+            query_lengths = torch.full((batch,), tokens, dtype=torch.int32)
+        if tokens > R.SHORT_THRESHOLD:
+            # wrap_triton (a pass-through outside torch.compile) rejects the interpreter's kernels
+            wrap = torch.library.wrap_triton
+            torch.library.wrap_triton = lambda kernel: kernel
+            try:
+                return R.long(qkv, b, a, conv, state, weight, A_log, dt_bias, query_lengths)
+            finally:
+                torch.library.wrap_triton = wrap
+        # the arguments of the reference's `short` wrapper (recurrent.py:192-231)
         value_heads = state.shape[1]
         key_heads = (qkv.shape[2] // R.DIM - value_heads) // 2
         qkv, b, a, conv, weight, A_log, dt_bias, state = (
@@ -236,13 +247,15 @@ def zero_state(geometry, rows, capacity):
 
 @torch.inference_mode()
 def run_schedule(step, geometry, state, schedule, capacity):
-    """schedule: list of per-step row token lists ([] = empty row). Returns per-step logits."""
+    """schedule: list of per-step row token lists ([] = empty row, several tokens = a prefill
+    chunk of that row). Returns per-step logits (of each row's last token)."""
     rows = len(schedule[0])
     positions = [0] * rows
     logits_all = []
     for tokens in schedule:
-        ids = torch.tensor([[t[0] if t else 0] for t in tokens], dtype=torch.int64)
-        pos = torch.tensor([[positions[r]] for r in range(rows)], dtype=torch.int64)
+        width = max(1, max(len(t) for t in tokens))
+        ids = torch.tensor([list(t) + [0] * (width - len(t)) for t in tokens], dtype=torch.int64)
+        pos = torch.tensor([[positions[r] + j for j in range(width)] for r in range(rows)], dtype=torch.int64)
         kv_lengths = torch.tensor([positions[r] + len(tokens[r]) for r in range(rows)], dtype=torch.int32)
         q_lengths = torch.tensor([len(t) for t in tokens], dtype=torch.int32)
         out = step(ids, pos, state, kv_lengths, q_lengths)
@@ -286,6 +299,9 @@ def make_schedules(geometry, kind, seed):
         return [[[tok()]] for _ in range(4)]
     if kind == "long16":
         return [[[tok()]] for _ in range(16)]
+    if kind == "prefill128":
+        # one 128-token prefill chunk (the reference's long DeltaNet path), then 4 decode steps
+        return [[[tok() for _ in range(128)]]] + [[[tok()]] for _ in range(4)]
     raise ValueError(kind)
 
 
@@ -297,6 +313,7 @@ CASES = {
     "qwen3.5-tiny-single": ("qwen3.5-tiny", "single", 16, 0.1, True),
     "qwen3.5-tiny-batch": ("qwen3.5-tiny", "batch", 16, 0.1, True),
     "qwen3.5-tiny-hv32-single": ("qwen3.5-tiny-hv32", "single", 16, 0.1, True),
+    "qwen3.5-tiny-prefill128": ("qwen3.5-tiny", "prefill128", 256, 0.1, True),
     "qwen3-0.6b-short": ("qwen3-0.6b", "short", 16, 0.0, False),
     "qwen3.5-0.8b-short": ("qwen3.5-0.8b", "short", 16, 0.0, False),
     # the headline geometry at the headline KV capacity: full depth, 4096 slots, 16 steps, the

@@ -19,7 +19,9 @@ LOGIT_COS = 0.9999
 STATE_REL = 1e-2
 
 
-def run_oracle(fx):
+def run_oracle(fx, dtype=torch.float32):
+    """The oracle over a fixture's schedule; a step whose single row carries several tokens (a
+    prefill chunk) is fed one token at a time, and its logits are the last token's."""
     g = configs.get(fx["config"])
     sd = synthetic.make_state_dict(g, seed=fx["seed"], jitter=fx["jitter"])
     W = O.prepare_weights(sd)
@@ -27,18 +29,23 @@ def run_oracle(fx):
     state = O.allocate_state(g, fx["capacity"], rows=rows)
     positions = [0] * rows
     logits = []
-    for tokens in fx["schedule"]:
-        ids = [t[0] if t else 0 for t in tokens]
-        kv = [positions[r] + len(tokens[r]) for r in range(rows)]
-        q = [len(t) for t in tokens]
-        out, state = O.decode_step(g, W, ids, positions[:], state, kv, q)
-        logits.append(out)
-        for r in range(rows):
-            positions[r] += len(tokens[r])
+    with O.accumulate(dtype):
+        for tokens in fx["schedule"]:
+            width = max(len(t) for t in tokens)
+            assert width <= 1 or rows == 1, "prefill chunks are single-row"
+            for j in range(max(1, width)):
+                ids = [t[j] if len(t) > j else 0 for t in tokens]
+                kv = [positions[r] + min(len(tokens[r]), j + 1) for r in range(rows)]
+                q = [1 if len(t) > j else 0 for t in tokens]
+                out, state = O.decode_step(g, W, ids, [positions[r] + j for r in range(rows)], state, kv, q)
+            logits.append(out)
+            for r in range(rows):
+                positions[r] += len(tokens[r])
     return g, torch.stack(logits), state, positions
 
 
-@pytest.mark.parametrize("name", [f for f in FIXTURES if "0.6b" not in f and "0.8b" not in f])
+@pytest.mark.parametrize("name", [f for f in FIXTURES if "0.6b" not in f and "0.8b" not in f
+                                  and "prefill" not in f])
 def test_oracle_matches_reference_fixture(name):
     fx = torch.load(GOLDEN / f"{name}.pt", weights_only=False)
     g, logits, state, positions = run_oracle(fx)
@@ -130,6 +137,28 @@ def test_noise_floor_record_matches_its_workload():
     assert (head["config"], head["capacity"], head["prompt"], head["decode"]) == ("qwen3.5-0.8b", 4096, 512, 8)
     assert len(head["per_step"]) == head["prompt"] + head["decode"]
     assert set(FLOOR["fixtures"]) >= {f for f in FIXTURES if "0.6b" in f or "0.8b" in f}
+
+
+@pytest.mark.parametrize("name", [f for f in FIXTURES if "prefill" in f])
+def test_oracle_matches_reference_prefill_fixture(name):
+    """The reference's own 128-token prefill chunk (its chunk-64 DeltaNet path, recurrent.py:234-281,
+    chunked.py) against the oracle's token-by-token recurrence: the same gated delta rule summed in
+    another order. Held to the north-star bar, or twice the spread of the oracle against its own
+    fp64-sum twin on this schedule where that is larger."""
+    fx = torch.load(GOLDEN / f"{name}.pt", weights_only=False)
+    g, logits, state, positions = run_oracle(fx)
+    _, twin, tstate, _ = run_oracle(fx, torch.float64)
+    assert positions == fx["positions"]
+    for s in range(len(fx["schedule"])):
+        a, b, c = logits[s, 0].float(), fx["logits"][s, 0].float(), twin[s, 0].float()
+        spread = (a - c).abs().max().item()
+        bound = max(LOGIT_MAX_ABS, 2 * spread)
+        assert ((a - b).abs() - (bound + b.abs() * 2.0 ** -7)).max().item() <= 0, (s, (a - b).abs().max().item())
+        assert O.cosine(a, b) >= min(LOGIT_COS, 1 - 2 * (1 - O.cosine(a, c))), s
+    for i, smp in enumerate(fx["state_sample"]):
+        got = state[i].reshape(-1)[smp["index"].long()]
+        tw = tstate[i].reshape(-1)[smp["index"].long()]
+        assert O.rel_l2(got.float(), smp["value"].float()) <= max(STATE_REL, 2 * O.rel_l2(tw.float(), got.float()) + 1e-3), i
 
 
 def test_attention_lower_right_causality_kat():

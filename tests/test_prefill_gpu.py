@@ -10,6 +10,7 @@ cascade, twice the spread that the oracle shows against its own fp64-sum twin on
 """
 
 import ctypes
+from pathlib import Path
 
 import pytest
 import torch
@@ -120,3 +121,43 @@ def test_runner_prefill_then_decode_matches_decode_only(cuda_device):
     lb = b.logits[0].float().cpu()
     assert O.cosine(la, lb) >= 0.9995 and (la - lb).abs().max().item() <= 0.1
     assert a.positions[0] == b.positions[0] == 300
+
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.mark.parametrize("fixture", sorted(p.stem for p in GOLDEN.glob("*.pt") if "prefill" in p.stem))
+def test_prefill_matches_reference_fixture(fixture, cuda_device):
+    """The reference's own prefill chunk (its chunk-64 DeltaNet path) and the decode steps after
+    it, against this library's prefill + decode: held to the north-star bar, or twice the oracle's
+    spread against its fp64-sum twin on the same schedule where that is larger."""
+    fx = torch.load(GOLDEN / f"{fixture}.pt", weights_only=False)
+    g, sd, W, eng = model(fx["config"], fx["capacity"], cuda_device)
+    assert fx["jitter"] == 0.1 and fx["seed"] == 0
+    state = [t.narrow(0, 0, 1) for t in eng.allocate_state()]
+    logits = torch.empty(g.vocab, dtype=torch.bfloat16, device=cuda_device)
+    tok = torch.empty(1, dtype=torch.int64, device=cuda_device)
+    # the oracle and its twin, token by token, for the bounds
+    prompt = [t for step in fx["schedule"] for t in step[0]]
+    want, _ = oracle_run(g, W, prompt, fx["capacity"])
+    twin, _ = oracle_run(g, W, prompt, fx["capacity"], torch.float64)
+    pos = 0
+    for s, step in enumerate(fx["schedule"]):
+        row = step[0]
+        if len(row) > 1:
+            eng.prefill(torch.tensor(row, dtype=torch.int64, device=cuda_device), pos, state, state, logits, tok)
+        else:
+            out = eng.decode_step(torch.tensor([[row[0]]], dtype=torch.int64, device=cuda_device),
+                                  torch.tensor([[pos]], dtype=torch.int64, device=cuda_device), state,
+                                  torch.tensor([pos + 1], dtype=torch.int32), torch.tensor([1], dtype=torch.int32),
+                                  next_tokens=tok)
+            logits.copy_(out[0][0])
+            state = list(out[1:])
+        pos += len(row)
+        got, ref = logits.float().cpu(), fx["logits"][s, 0].float()
+        spread = (want[pos - 1].float() - twin[pos - 1].float()).abs().max().item()
+        bound = max(LOGIT_MAX_ABS, 2 * spread)
+        assert ((got - ref).abs() - (bound + ref.abs() * 2.0 ** -7)).max().item() <= 0, (s, (got - ref).abs().max().item())
+        assert O.cosine(got, ref) >= min(LOGIT_COS, 1 - 2 * (1 - O.cosine(want[pos - 1], twin[pos - 1])))
+        assert int(tok[0]) == int(torch.argmax(got))
+    eng.check_prefill_error()

@@ -102,10 +102,18 @@ QWEN3_0_6B_L2 = replace(QWEN3_0_6B, name="qwen3-0.6b-l2", num_layers=2, layer_ty
 QWEN35_0_8B_L4 = replace(QWEN35_0_8B, name="qwen3.5-0.8b-l4", num_layers=4, layer_types=())
 QWEN35_4B_L4 = replace(QWEN35_4B, name="qwen3.5-4b-l4", num_layers=4, layer_types=())
 
+# The smallest geometry the kernels take (one DeltaNet and one attention layer, one key / two
+# value DeltaNet heads): for format tests whose fixtures are committed (a bundle archive).
+QWEN35_MICRO = replace(
+    QWEN35_0_8B, name="qwen3.5-micro", num_layers=2, hidden=256, intermediate=64, vocab=128,
+    num_q_heads=2, num_kv_heads=1, lin_key_heads=1, lin_value_heads=2, full_attention_interval=2,
+    layer_types=(),
+)
+
 CONFIGS = {
     g.name: g
     for g in (QWEN3_0_6B, QWEN35_0_8B, QWEN35_4B, QWEN3_TINY, QWEN35_TINY, QWEN35_TINY_HV32,
-              QWEN3_0_6B_L2, QWEN35_0_8B_L4, QWEN35_4B_L4)
+              QWEN3_0_6B_L2, QWEN35_0_8B_L4, QWEN35_4B_L4, QWEN35_MICRO)
 }
 
 
