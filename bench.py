@@ -139,10 +139,11 @@ def prefill_flops(g, chunks):
 def measure_prefill(args, dist, dev, world, rank):
     """Prefill throughput of the prompt in 512-token chunks."""
     from xinfer_b200 import configs, synthetic
-    from xinfer_b200.engine import Engine
+    from xinfer_b200.engine import Engine, pack_linears
 
     g = configs.get(args.config)
-    weights = synthetic.make_state_dict(g, seed=0, device=dev)
+    # the reference bundle's layout: each projection group as adjacent rows of one tensor
+    weights = pack_linears(g, synthetic.make_state_dict(g, seed=0, device=dev))
     eng = Engine(g, weights, capacity=args.capacity, device=dev)
     prompt = synthetic.random_prompt(g, args.prompt, seed=1000 + rank)
     ids = torch.tensor(prompt, dtype=torch.int64).to(dev)
@@ -463,10 +464,10 @@ def main():
         return measure_prefill(args, dist, dev, world, rank)
 
     from xinfer_b200 import configs, synthetic
-    from xinfer_b200.engine import Engine, Runner
+    from xinfer_b200.engine import Engine, Runner, pack_linears
 
     g = configs.get(args.config)
-    weights = synthetic.make_state_dict(g, seed=0, device=dev)
+    weights = pack_linears(g, synthetic.make_state_dict(g, seed=0, device=dev))
     eng = Engine(g, weights, capacity=args.capacity, device=dev)
     runner = Runner(eng)
     B = args.batch

@@ -18,7 +18,7 @@ import torch
 from oracle import qwen_step as O
 from xinfer_b200 import _native as nat
 from xinfer_b200 import configs, synthetic
-from xinfer_b200.engine import Engine, Runner
+from xinfer_b200.engine import Engine, Runner, pack_linears
 
 pytestmark = pytest.mark.gpu
 
@@ -37,7 +37,8 @@ def model(name, capacity, device):
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 1024, 1024), (7, 8224, 1024), (128, 3584, 1024), (300, 1024, 3584),
-                                   (512, 2048, 2560), (1, 151936, 1024), (513, 24, 64)])
+                                   (512, 2048, 2560), (1, 151936, 1024), (513, 24, 64), (37, 5, 64),
+                                   (512, 2, 1024)])
 def test_gemm_matches_fp32_product(m, n, k, cuda_device):
     torch.backends.cuda.matmul.allow_tf32 = False
     gen = torch.Generator(device=cuda_device).manual_seed(m * 7 + n)
@@ -105,6 +106,25 @@ def test_prefill_matches_token_by_token_oracle(name, T, chunks, cuda_device):
             assert torch.count_nonzero(a0[:, :, T:]) == 0 and torch.count_nonzero(a1[:, :, T:]) == 0
         for a, b, c in pairs:
             assert O.rel_l2(a, b) <= max(STATE_REL, 2 * O.rel_l2(c, b)), f"{name} T={T} state of layer {i}"
+
+
+def test_packed_projections_give_the_same_prefill(cuda_device):
+    """Weights in the reference's packed layout (each projection group as adjacent rows of one
+    tensor) run one GEMM per group; the result equals the per-projection GEMMs bit for bit."""
+    g, sd, W, eng = model("qwen3.5-0.8b-l4", 640, cuda_device)
+    packed = Engine(g, pack_linears(g, {k: v.to(cuda_device) for k, v in sd.items()}), capacity=640,
+                    device=cuda_device)
+    prompt = torch.tensor(synthetic.random_prompt(g, 200, seed=5), dtype=torch.int64, device=cuda_device)
+    outs = []
+    for e in (eng, packed):
+        state = [t.narrow(0, 0, 1) for t in e.allocate_state()]
+        logits = torch.empty(g.vocab, dtype=torch.bfloat16, device=cuda_device)
+        e.prefill(prompt, 0, state, state, logits)
+        e.check_prefill_error()
+        outs.append([logits] + [t.clone() for t in state])
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    packed.close()
 
 
 def test_runner_prefill_then_decode_matches_decode_only(cuda_device):

@@ -15,7 +15,10 @@
 #include "cutlass/gemm/kernel/gemm_universal.hpp"
 #include "cutlass/util/packed_stride.hpp"
 
+#include <cstring>
+#include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "xb_host.h"
 
@@ -45,19 +48,89 @@ using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, M
 using Gemm = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
 } // namespace xbgemm
 
-extern "C" int xb_gemm_bf16(int32_t m, int32_t n, int32_t k, const void *x, const void *w, void *out,
-                            void *stream) {
+namespace {
+// Launch parameters (TMA descriptors included) of every (shape, operands, device) seen: a prefill
+// chunk runs the same GEMMs on the same buffers again and again, and building the descriptors is
+// host work comparable to the kernel itself at these sizes.
+struct PlanKey {
+  int m, n, k, device;
+  long long ldo;
+  const void *x, *w;
+  void *out;
+  bool operator==(const PlanKey &o) const { return std::memcmp(this, &o, sizeof(PlanKey)) == 0; }
+};
+struct PlanHash {
+  size_t operator()(const PlanKey &p) const {
+    size_t h = 1469598103934665603ull;
+    const unsigned char *b = reinterpret_cast<const unsigned char *>(&p);
+    for (size_t i = 0; i < sizeof(PlanKey); ++i) h = (h ^ b[i]) * 1099511628211ull;
+    return h;
+  }
+};
+constexpr size_t kMaxPlans = 4096;
+std::mutex plan_mu;
+std::unordered_map<PlanKey, xbgemm::Gemm::Params, PlanHash> plans;
+
+// out[m, n] = x[m, :] . w[n, :] for shapes the tensor-core kernel cannot take (n not a multiple
+// of 8): one warp per output element, fp32 sum, one rounding.
+__global__ void gemm_rows_kernel(int m, int n, int k, const __nv_bfloat16 *x, const __nv_bfloat16 *w,
+                                 __nv_bfloat16 *out, long long ldo) {
+  const long long e = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (e >= (long long)m * n) return;
+  const int row = (int)(e / n), col = (int)(e % n);
+  const uint4 *a = reinterpret_cast<const uint4 *>(x + (long long)row * k);
+  const uint4 *b = reinterpret_cast<const uint4 *>(w + (long long)col * k);
+  float acc = 0.f;
+  for (int c = lane; c < k / 8; c += 32) {
+    const uint4 av = a[c], bv = b[c];
+    const __nv_bfloat162 *ap = reinterpret_cast<const __nv_bfloat162 *>(&av);
+    const __nv_bfloat162 *bp = reinterpret_cast<const __nv_bfloat162 *>(&bv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 af = __bfloat1622float2(ap[i]), bf = __bfloat1622float2(bp[i]);
+      acc = fmaf(af.x, bf.x, acc);
+      acc = fmaf(af.y, bf.y, acc);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) out[(long long)row * ldo + col] = __float2bfloat16_rn(acc);
+}
+} // namespace
+
+int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, long long ldo, void *stream) {
   using namespace xbgemm;
-  if (m < 1 || n < 1 || k < 1 || !x || !w || !out) return xb::fail(XB_ERR_INVALID, "invalid GEMM arguments");
-  if (n % kAlign || k % kAlign) return xb::fail(XB_ERR_INVALID, "GEMM N and K must be multiples of 8");
-  if (((uintptr_t)x | (uintptr_t)w | (uintptr_t)out) & 15)
-    return xb::fail(XB_ERR_INVALID, "GEMM operands must be 16-byte aligned");
+  if (m < 1 || n < 1 || k < 1 || !x || !w || !out || ldo < n) return xb::fail(XB_ERR_INVALID, "invalid GEMM arguments");
+  if (k % kAlign) return xb::fail(XB_ERR_INVALID, "GEMM K must be a multiple of 8");
+  if (((uintptr_t)x | (uintptr_t)w) & 15) return xb::fail(XB_ERR_INVALID, "GEMM operands must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n % kAlign || ldo % kAlign || ((uintptr_t)out & 15)) {
+    const long long total = (long long)m * n;
+    gemm_rows_kernel<<<(unsigned)((total + 7) / 8), 256, 0, st>>>(m, n, k, static_cast<const __nv_bfloat16 *>(x),
+                                                                 static_cast<const __nv_bfloat16 *>(w),
+                                                                 static_cast<__nv_bfloat16 *>(out), ldo);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? XB_OK : xb::fail(XB_ERR_CUDA, std::string("GEMM launch: ") + cudaGetErrorString(e));
+  }
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return xb::fail(XB_ERR_CUDA, "GEMM: no current device");
+  const PlanKey key{m, n, k, device, ldo, x, w, out};
+  {
+    std::lock_guard<std::mutex> lock(plan_mu);
+    auto it = plans.find(key);
+    if (it != plans.end()) {
+      if (Gemm::run(it->second, st) != cutlass::Status::kSuccess) return xb::fail(XB_ERR_CUDA, "GEMM launch failed");
+      return XB_OK;
+    }
+  }
   using SA = typename Kernel::StrideA;
   using SB = typename Kernel::StrideB;
   using SD = typename Kernel::StrideD;
   const SA sa = cutlass::make_cute_packed_stride(SA{}, make_shape(m, k, 1));
   const SB sb = cutlass::make_cute_packed_stride(SB{}, make_shape(n, k, 1));
-  const SD sd = cutlass::make_cute_packed_stride(SD{}, make_shape(m, n, 1));
+  SD sd = cutlass::make_cute_packed_stride(SD{}, make_shape(m, n, 1));
+  cute::get<0>(sd) = ldo;
   typename Gemm::Arguments args{cutlass::gemm::GemmUniversalMode::kGemm,
                                 {m, n, k, 1},
                                 {static_cast<const ElementA *>(x), sa, static_cast<const ElementB *>(w), sb},
@@ -66,9 +139,16 @@ extern "C" int xb_gemm_bf16(int32_t m, int32_t n, int32_t k, const void *x, cons
   if (gemm.can_implement(args) != cutlass::Status::kSuccess)
     return xb::fail(XB_ERR_UNSUPPORTED, "GEMM shape not supported by the sm_100 kernel");
   if (Gemm::get_workspace_size(args) != 0) return xb::fail(XB_ERR_UNSUPPORTED, "GEMM needs a workspace");
-  if (gemm.initialize(args, nullptr, static_cast<cudaStream_t>(stream)) != cutlass::Status::kSuccess)
+  if (gemm.initialize(args, nullptr, st) != cutlass::Status::kSuccess)
     return xb::fail(XB_ERR_CUDA, "GEMM initialisation failed");
-  if (gemm.run(static_cast<cudaStream_t>(stream)) != cutlass::Status::kSuccess)
-    return xb::fail(XB_ERR_CUDA, "GEMM launch failed");
+  if (gemm.run(st) != cutlass::Status::kSuccess) return xb::fail(XB_ERR_CUDA, "GEMM launch failed");
+  std::lock_guard<std::mutex> lock(plan_mu);
+  if (plans.size() >= kMaxPlans) plans.clear();
+  plans.emplace(key, gemm.params());
   return XB_OK;
+}
+
+extern "C" int xb_gemm_bf16(int32_t m, int32_t n, int32_t k, const void *x, const void *w, void *out,
+                            void *stream) {
+  return xb::gemm_bf16(m, n, k, x, w, out, n, stream);
 }

@@ -27,22 +27,34 @@ namespace xbpre {
 using namespace xb;
 
 constexpr int kMaxTokens = 512;
+constexpr int kChunk = 32;  // tokens per step of the chunked gated delta rule
+// per (chunk, head): T^-1 and M (column-major, [j][i]), A_i, beta_i, A_32 / A_j, A_32
+constexpr int kRecFloats = 2 * kChunk * kChunk + 3 * kChunk + 32;
 // the prefill workspace starts with the decode workspace's control words, so that
 // xb_workspace_check reads its error word (word 64) the same way
 constexpr int kCtlBytes = 1024;
 enum { PERR_TOKEN = 4 };
 
 struct Layout {
-  size_t h, x, x2, out, qkv, z, bb, aa, gate, up, qn, kn, vv, beta, decay, core, qatt, oatt, xlast, total;
+  size_t h, x, x2, out, proj, qn, kn, vv, beta, glog, rec, core, qatt, oatt, xlast, total;
 };
 
 static int lin_channels(const XbGeometry &g) { return (2 * g.lin_key_heads + g.lin_value_heads) * g.lin_head_dim; }
+
+// Row width of the projection buffer: the widest group of projections that read one input
+// (DeltaNet qkv | z | b | a, attention q | k | v, MLP gate | up), each group's outputs side by side
+// in one row per token, as the reference's packed linears produce them (pack_linears.py).
+static int proj_width(const XbGeometry &g) {
+  const bool q35 = g.family == XB_FAMILY_QWEN35;
+  const int delta = q35 ? lin_channels(g) + g.lin_value_heads * g.lin_head_dim + 2 * g.lin_value_heads : 0;
+  const int attn = g.num_q_heads * g.head_dim * (q35 ? 2 : 1) + 2 * g.num_kv_heads * g.head_dim;
+  return std::max({delta, attn, 2 * g.intermediate});
+}
 
 static Layout layout(const XbGeometry &g, int T) {
   Layout L{};
   const bool q35 = g.family == XB_FAMILY_QWEN35;
   const int HVD = q35 ? g.lin_value_heads * g.lin_head_dim : 0;
-  const int qrows = g.num_q_heads * g.head_dim * (q35 ? 2 : 1);
   const int widest = std::max({g.hidden, g.intermediate, g.num_q_heads * g.head_dim, HVD});
   size_t off = kCtlBytes;
   auto take = [&](size_t bytes) { size_t o = off; off += (bytes + 255) & ~size_t(255); return o; };
@@ -50,18 +62,14 @@ static Layout layout(const XbGeometry &g, int T) {
   L.x = take((size_t)T * widest * 2);
   L.x2 = take((size_t)T * widest * 2);
   L.out = take((size_t)T * g.hidden * 2);
-  L.qkv = take((size_t)T * std::max(q35 ? lin_channels(g) : 0, qrows) * 2);
-  L.z = take((size_t)T * std::max(HVD, g.num_kv_heads * g.head_dim) * 2);
-  L.bb = take((size_t)T * std::max(q35 ? g.lin_value_heads : 8, g.num_kv_heads * g.head_dim) * 2);
-  L.aa = take((size_t)T * std::max(q35 ? g.lin_value_heads : 8, 8) * 2);
-  L.gate = take((size_t)T * g.intermediate * 2);
-  L.up = take((size_t)T * g.intermediate * 2);
+  L.proj = take((size_t)T * proj_width(g) * 2);
   const size_t vec = q35 ? (size_t)T * HVD * 4 : 256;
   L.qn = take(vec);
   L.kn = take(vec);
   L.vv = take(vec);
   L.beta = take(q35 ? (size_t)T * g.lin_value_heads * 4 : 256);
-  L.decay = take(q35 ? (size_t)T * g.lin_value_heads * 4 : 256);
+  L.glog = take(q35 ? (size_t)T * g.lin_value_heads * 4 : 256);
+  L.rec = take(q35 ? (size_t)((T + kChunk - 1) / kChunk) * g.lin_value_heads * kRecFloats * 4 : 256);
   L.core = take(q35 ? (size_t)T * HVD * 2 : 256);
   L.qatt = take((size_t)T * g.num_q_heads * g.head_dim * 2);
   L.oatt = take((size_t)T * g.num_q_heads * g.head_dim * 2);
@@ -82,12 +90,16 @@ __global__ void embed_kernel(const int64_t *ids, const bf16 *embed, bf16 *h, int
   for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = ok ? src[c] : make_uint4(0, 0, 0, 0);
 }
 
-// RMSNorm of rows (HF Qwen3RMSNorm: w * bf16(x r); Qwen3_5RMSNorm: bf16(x r (1 + w))), 256
-// threads per row, each summing the squares of its 8-element chunks c and c + 256 in order.
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const bf16 *in, const bf16 *w, bf16 *out, int H,
-                                                      float eps, int q35) {
-  const int t = blockIdx.x, tid = threadIdx.x, nc = H / 8;
-  const uint4 *row = reinterpret_cast<const uint4 *>(in + (long long)t * H);
+// Residual add and RMSNorm of rows: with `o`, h = bf16(h + o) first (the reference's residual
+// add, both operands bf16) and h is written back; then out = RMSNorm(h) (HF Qwen3RMSNorm:
+// w * bf16(x r); Qwen3_5RMSNorm: bf16(x r (1 + w))). 256 threads per row, each summing the
+// squares of its 8-element chunks c and c + 256 in order. Row blockIdx.x + row0 of h is
+// normalised into row blockIdx.x of out.
+__global__ void __launch_bounds__(256) add_rmsnorm_kernel(bf16 *h, const bf16 *o, const bf16 *w, bf16 *out, int H,
+                                                          float eps, int q35, int row0) {
+  const int t = blockIdx.x + row0, tid = threadIdx.x, nc = H / 8;
+  uint4 *row = reinterpret_cast<uint4 *>(h + (long long)t * H);
+  const uint4 *orow = o ? reinterpret_cast<const uint4 *>(o + (long long)t * H) : nullptr;
   __shared__ float red[8];
   uint4 xv[2];
   float ss = 0.f;
@@ -97,6 +109,14 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const bf16 *in, const bf16
     xv[i] = c < nc ? row[c] : make_uint4(0, 0, 0, 0);
     float x[8];
     unpack8(xv[i], x);
+    if (orow && c < nc) {
+      float y[8];
+      unpack8(orow[c], y);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = rbf(x[e] + y[e]);
+      xv[i] = make_uint4(pack2(x[0], x[1]), pack2(x[2], x[3]), pack2(x[4], x[5]), pack2(x[6], x[7]));
+      row[c] = xv[i];
+    }
 #pragma unroll
     for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
   }
@@ -107,7 +127,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const bf16 *in, const bf16
 #pragma unroll
   for (int i = 0; i < 8; ++i) tot += red[i];
   const float r = rsqrtf(tot / (float)H + eps);
-  uint4 *dst = reinterpret_cast<uint4 *>(out + (long long)t * H);
+  uint4 *dst = reinterpret_cast<uint4 *>(out + (long long)blockIdx.x * H);
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int c = tid + i * 256;
@@ -121,40 +141,43 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const bf16 *in, const bf16
   }
 }
 
-// h = bf16(h + o), the residual adds of the reference (both operands bf16).
-__global__ void add_kernel(bf16 *h, const bf16 *o, long long n) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n / 2; i += (long long)gridDim.x * blockDim.x) {
-    const uint32_t a = reinterpret_cast<uint32_t *>(h)[i], b = reinterpret_cast<const uint32_t *>(o)[i];
-    reinterpret_cast<uint32_t *>(h)[i] = pack2(bf_lo(a) + bf_lo(b), bf_hi(a) + bf_hi(b));
-  }
-}
-
-// act = bf16(bf16(silu(gate)) * up) (HF SiLU on a bf16 tensor, then the bf16 product).
-__global__ void silu_mul_kernel(const bf16 *gate, const bf16 *up, bf16 *act, long long n) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const float g = bf(gate[i]), u = bf(up[i]);
-    const float s = rbf(g / (1.f + expf(-g)));
-    act[i] = tobf(s * u);
+// act = bf16(bf16(silu(gate)) * up) (HF SiLU on a bf16 tensor, then the bf16 product), 8 values
+// per thread; gate and up are the two halves of each [gate | up] projection row.
+__global__ void silu_mul_kernel(const bf16 *proj, bf16 *act, int I, int ld, int T) {
+  const int n8 = I / 8;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)T * n8;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long t = i / n8;
+    const int c = (int)(i % n8);
+    const uint4 gv = reinterpret_cast<const uint4 *>(proj + t * ld)[c];
+    const uint4 uv = reinterpret_cast<const uint4 *>(proj + t * ld + I)[c];
+    float g[8], u[8], y[8];
+    unpack8(gv, g);
+    unpack8(uv, u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = rbf(g[e] / (1.f + expf(-g[e]))) * u[e];
+    reinterpret_cast<uint4 *>(act + t * I)[c] =
+        make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]), pack2(y[6], y[7]));
   }
 }
 
 // DeltaNet preparation of token t, value head h (recurrent.py:32-58, 99-120 and the prepare step
 // of the long path, recurrent.py:127-189): width-4 causal conv over [old window, tokens] with fp32
 // FMAs in tap order, bf16, SiLU, bf16; q, k l2-normalised (q also scaled by dk^-0.5); beta =
-// bf16(sigmoid(b)); decay = exp(-exp(A_log) * softplus(a + dt_bias)), softplus threshold 20.
+// bf16(sigmoid(b)); the log decay g = -exp(A_log) * softplus(a + dt_bias), softplus threshold 20.
 __global__ void __launch_bounds__(256) delta_prepare_kernel(
-    const bf16 *qkv, const bf16 *bb, const bf16 *aa, const bf16 *conv_in, const bf16 *conv_w,
-    const bf16 *a_log, const bf16 *dt_bias, float *qn, float *kn, float *vv, float *beta, float *decay,
+    const bf16 *qkv, const bf16 *bb, const bf16 *aa, int ld, const bf16 *conv_in, const bf16 *conv_w,
+    const bf16 *a_log, const bf16 *dt_bias, float *qn, float *kn, float *vv, float *beta, float *glog,
     int HK, int HV, int DK, float dk_scale) {
   const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
-  const int CH = (2 * HK + HV) * DK, kh = h / (HV / HK);
+  const int kh = h / (HV / HK);
   __shared__ float pn[8];
   auto conv = [&](int ch) -> float {
     float tot = 0.f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int s = t - 3 + j;
-      const float in = s < 0 ? bf(conv_in[(long long)ch * 4 + 4 + s]) : bf(qkv[(long long)s * CH + ch]);
+      const float in = s < 0 ? bf(conv_in[(long long)ch * 4 + 4 + s]) : bf(qkv[(long long)s * ld + ch]);
       tot = fmaf(in, bf(conv_w[(long long)ch * 4 + j]), tot);
     }
     const float v = rbf(tot);
@@ -177,99 +200,240 @@ __global__ void __launch_bounds__(256) delta_prepare_kernel(
     kn[base + tid - DK] = val * ks;
   }
   if (tid == 0) {
-    const float b = bf(bb[(long long)t * HV + h]), a = bf(aa[(long long)t * HV + h]);
+    const float b = bf(bb[(long long)t * ld + h]), a = bf(aa[(long long)t * ld + h]);
     beta[(long long)t * HV + h] = rbf(1.f / (1.f + expf(-b)));
     const float x = a + bf(dt_bias[h]);
     const float sp = x > 20.f ? x : log1pf(expf(x));
-    decay[(long long)t * HV + h] = expf(-expf(bf(a_log[h])) * sp);
+    glog[(long long)t * HV + h] = -expf(bf(a_log[h])) * sp;
   }
 }
 
 // The conv window after the last token: the last four inputs of [old window, tokens] for every
 // channel (recurrent.py:43-52). Launched after every read of the old window, so in place is safe.
-__global__ void conv_state_kernel(const bf16 *qkv, const bf16 *conv_in, bf16 *conv_out, int CH, int T) {
+__global__ void conv_state_kernel(const bf16 *qkv, int ld, const bf16 *conv_in, bf16 *conv_out, int CH, int T) {
   const int ch = blockIdx.x * blockDim.x + threadIdx.x;
   if (ch >= CH) return;
   bf16 w[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int s = T - 4 + j;
-    w[j] = s < 0 ? conv_in[(long long)ch * 4 + 4 + s] : qkv[(long long)s * CH + ch];
+    w[j] = s < 0 ? conv_in[(long long)ch * 4 + 4 + s] : qkv[(long long)s * ld + ch];
   }
 #pragma unroll
   for (int j = 0; j < 4; ++j) conv_out[(long long)ch * 4 + j] = w[j];
 }
 
-// Gated delta rule over T tokens (recurrent.py:20-28) for one value head and 16 columns of its
-// 128 x 128 fp32 state: warp w owns columns 2w, 2w + 1, lane l rows 4l..4l + 3. Per token:
-// S *= decay; delta = (v - S^T k) * beta; S += k delta^T; out = S^T q (bf16). The next token's
-// inputs are loaded while the current one is processed.
-__global__ void __launch_bounds__(256) delta_scan_kernel(const float *qn, const float *kn, const float *vv,
-                                                         const float *beta, const float *decay,
-                                                         const float *rec_in, float *rec_out, bf16 *core,
-                                                         int HV, int DK, int T) {
-  const int h = blockIdx.x, tile = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c0 = tile * 16 + 2 * warp, r0 = lane * 4;
-  const float *Si = rec_in + (long long)h * DK * DK;
-  float S[4][2];
+// ---- chunked gated delta rule ---------------------------------------------------------------
+// The recurrence (recurrent.py:20-28), per value head with state S [dk, dv] fp32:
+//   S_i = a_i S_{i-1} + k_i d_i^T,  d_i = b_i (v_i - a_i S_{i-1}^T k_i),  o_i = S_i^T q_i,
+// evaluated 32 tokens at a time in the closed form of the reference's chunked path
+// (chunked.py:17-160; chunk 64 there): with A_i = a_1 ... a_i inside the chunk,
+//   (I + L) d = beta (v - A pk),  L_ij = beta_i (A_i / A_j) k_i.k_j  (j < i),  pk_i = k_i . S_0,
+//   o_i = A_i q_i . S_0 + sum_{j<=i} (A_i / A_j) (q_i . k_j) d_j,
+//   S_32 = A_32 S_0 + sum_j (A_32 / A_j) k_j d_j^T.
+// A_i / A_j = exp(P_i - P_j) with P the in-order prefix sum of the log decays g. Tokens past the
+// prompt are zero (g = 0, beta = 0, k = q = v = 0), which leaves S and every real token unchanged.
+enum { REC_TINV = 0, REC_MO = kChunk * kChunk, REC_A = 2 * kChunk * kChunk, REC_BETA = REC_A + kChunk,
+       REC_WS = REC_BETA + kChunk, REC_ALAST = REC_WS + kChunk };
+
+// The chunk-local matrices of one (chunk, head), all from the keys, queries, gates and betas:
+// P, the Gram matrices k_i.k_j and q_i.k_j, T^-1 = (I + L)^-1 by forward substitution
+// (reference: _solve, chunked.py:17-44), M_ij = (A_i / A_j) q_i.k_j (j <= i).
+__global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float *qn, const float *kn, const float *glog,
+                                                               const float *beta, float *rec, int HV, int DK, int T) {
+  const int chunk = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t0 = chunk * kChunk;
+  __shared__ float ks[kChunk][129], qs[kChunk][129];
+  __shared__ float P[kChunk], bt[kChunk], Lm[kChunk][kChunk + 1], Qm[kChunk][kChunk + 1];
+  for (int idx = tid; idx < kChunk * DK; idx += blockDim.x) {
+    const int t = idx / DK, d = idx % DK, tok = t0 + t;
+    const long long src = ((long long)tok * HV + h) * DK + d;
+    ks[t][d] = tok < T ? kn[src] : 0.f;
+    qs[t][d] = tok < T ? qn[src] : 0.f;
+  }
+  if (tid < kChunk) {
+    const int tok = t0 + tid;
+    P[tid] = tok < T ? glog[(long long)tok * HV + h] : 0.f;
+    bt[tid] = tok < T ? beta[(long long)tok * HV + h] : 0.f;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float run = 0.f;
+    for (int i = 0; i < kChunk; ++i) { run += P[i]; P[i] = run; }
+  }
+  // Gram rows i = 4 warp .. 4 warp + 3 against key j = lane, summed over d in order
+  float ag[4] = {0.f, 0.f, 0.f, 0.f}, aq[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int d = 0; d < DK; ++d) {
+    const float kj = ks[lane][d];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      ag[r] = fmaf(ks[warp * 4 + r][d], kj, ag[r]);
+      aq[r] = fmaf(qs[warp * 4 + r][d], kj, aq[r]);
+    }
+  }
+  __syncthreads();  // P complete
+  float *out = rec + ((long long)chunk * HV + h) * kRecFloats;
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
-    S[r][0] = Si[(long long)(r0 + r) * DK + c0];
-    S[r][1] = Si[(long long)(r0 + r) * DK + c0 + 1];
+    const int i = warp * 4 + r, j = lane;
+    const float ratio = j <= i ? expf(P[i] - P[j]) : 0.f;
+    Lm[i][j] = j < i ? bt[i] * ratio * ag[r] : 0.f;
+    Qm[i][j] = j <= i ? ratio * aq[r] : 0.f;
   }
-  auto load = [&](int t, float4 &k4, float4 &q4, float2 &v2, float &bt, float &dc) {
-    const long long base = ((long long)t * HV + h) * DK;
-    k4 = *reinterpret_cast<const float4 *>(kn + base + r0);
-    q4 = *reinterpret_cast<const float4 *>(qn + base + r0);
-    v2 = *reinterpret_cast<const float2 *>(vv + base + c0);
-    bt = beta[(long long)t * HV + h];
-    dc = decay[(long long)t * HV + h];
+  __syncthreads();
+  for (int idx = tid; idx < kChunk * kChunk; idx += blockDim.x) {
+    const int j = idx / kChunk, i = idx % kChunk;
+    out[REC_MO + idx] = Qm[i][j];
+  }
+  if (tid < kChunk) {
+    out[REC_A + tid] = expf(P[tid]);
+    out[REC_BETA + tid] = bt[tid];
+    out[REC_WS + tid] = expf(P[kChunk - 1] - P[tid]);
+    if (tid == 0) out[REC_ALAST] = expf(P[kChunk - 1]);
+  }
+  if (warp == 0) {
+    // row i of X = (I + L)^-1: X_i = e_i - sum_{j<i} L_ij X_j; lane c keeps column c of X
+    float X[kChunk];
+#pragma unroll
+    for (int i = 0; i < kChunk; ++i) {
+      float x = lane == i ? 1.f : 0.f;
+#pragma unroll
+      for (int j = 0; j < i; ++j) x = fmaf(-Lm[i][j], X[j], x);
+      X[i] = x;
+    }
+#pragma unroll
+    for (int i = 0; i < kChunk; ++i) out[REC_TINV + lane * kChunk + i] = X[i];
+  }
+}
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool valid) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// One CTA per (value head, 8 value columns), warp w owns column 8 blockIdx.y + w, lane l rows
+// 4l..4l + 3 of it. Per chunk (double-buffered in shared memory by cp.async): 32 key and query
+// projections of S_0 per lane, summed across the warp by a transposing butterfly (lane i ends with
+// token i's sums), then d = T^-1 rhs and o by broadcasts, then the state update.
+struct ChunkBuf {
+  float k[kChunk][128];
+  float q[kChunk][128];
+  float v[kChunk][8];
+  float rec[kRecFloats];
+};
+constexpr size_t kScanSmem = 2 * sizeof(ChunkBuf) + kChunk * 8 * sizeof(float);
+
+__device__ __forceinline__ void transpose_sum(float (&v)[kChunk], int lane) {
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool up = lane & s;
+#pragma unroll
+    for (int j = 0; j < s; ++j) {
+      const float send = up ? v[j] : v[j + s];
+      const float keep = up ? v[j + s] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256, 2) delta_chunk_scan_kernel(const float *qn, const float *kn, const float *vv,
+                                                               const float *rec, const float *rec_in, float *rec_out,
+                                                               bf16 *core, int HV, int T) {
+  constexpr int DK = 128;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  ChunkBuf *buf = reinterpret_cast<ChunkBuf *>(smem_raw);
+  float(*obuf)[8] = reinterpret_cast<float(*)[8]>(smem_raw + 2 * sizeof(ChunkBuf));
+  const int h = blockIdx.x, c0 = blockIdx.y * 8, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c = c0 + warp, r0 = lane * 4;
+  const int nch = (T + kChunk - 1) / kChunk;
+  auto issue = [&](int chunk, ChunkBuf &b) {
+    const int t0 = chunk * kChunk;
+    for (int idx = tid; idx < kChunk * DK / 4; idx += 256) {
+      const int t = idx / (DK / 4), d4 = idx % (DK / 4), tok = t0 + t;
+      const long long src = ((long long)min(tok, T - 1) * HV + h) * DK + d4 * 4;
+      cp_async16(&b.k[t][d4 * 4], kn + src, tok < T);
+      cp_async16(&b.q[t][d4 * 4], qn + src, tok < T);
+    }
+    if (tid < kChunk * 2) {
+      const int t = tid >> 1, half = tid & 1, tok = t0 + t;
+      cp_async16(&b.v[t][half * 4], vv + ((long long)min(tok, T - 1) * HV + h) * DK + c0 + half * 4, tok < T);
+    }
+    const float *src = rec + ((long long)chunk * HV + h) * kRecFloats;
+    for (int idx = tid; idx < kRecFloats / 4; idx += 256) cp_async16(&b.rec[idx * 4], src + idx * 4, true);
+    cp_async_commit();
   };
-  float4 k4, q4, nk4, nq4;
-  float2 v2, nv2;
-  float bt, dc, nbt, ndc;
-  load(0, k4, q4, v2, bt, dc);
-  for (int t = 0; t < T; ++t) {
-    if (t + 1 < T) load(t + 1, nk4, nq4, nv2, nbt, ndc);
-    const float k[4] = {k4.x, k4.y, k4.z, k4.w}, q[4] = {q4.x, q4.y, q4.z, q4.w};
-    float p0 = 0.f, p1 = 0.f;
+  const float *Si = rec_in + (long long)h * DK * DK;
+  float S[4];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      S[r][0] *= dc;
-      S[r][1] *= dc;
-      p0 = fmaf(S[r][0], k[r], p0);
-      p1 = fmaf(S[r][1], k[r], p1);
+  for (int r = 0; r < 4; ++r) S[r] = Si[(long long)(r0 + r) * DK + c];
+  issue(0, buf[0]);
+  for (int ch = 0; ch < nch; ++ch) {
+    if (ch + 1 < nch) {
+      issue(ch + 1, buf[(ch + 1) & 1]);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
-    p0 = warp_sum(p0);
-    p1 = warp_sum(p1);
-    const float d0 = (v2.x - p0) * bt, d1 = (v2.y - p1) * bt;
-    float o0 = 0.f, o1 = 0.f;
+    __syncthreads();
+    const ChunkBuf &b = buf[ch & 1];
+    float pk[kChunk], pq[kChunk];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      S[r][0] = fmaf(k[r], d0, S[r][0]);
-      S[r][1] = fmaf(k[r], d1, S[r][1]);
-      o0 = fmaf(S[r][0], q[r], o0);
-      o1 = fmaf(S[r][1], q[r], o1);
+    for (int i = 0; i < kChunk; ++i) {
+      const float4 kv = *reinterpret_cast<const float4 *>(&b.k[i][r0]);
+      pk[i] = fmaf(kv.w, S[3], fmaf(kv.z, S[2], fmaf(kv.y, S[1], kv.x * S[0])));
     }
-    o0 = warp_sum(o0);
-    o1 = warp_sum(o1);
-    if (lane == 0)
-      *reinterpret_cast<uint32_t *>(core + ((long long)t * HV + h) * DK + c0) = pack2(o0, o1);
-    k4 = nk4; q4 = nq4; v2 = nv2; bt = nbt; dc = ndc;
+    transpose_sum(pk, lane);
+#pragma unroll
+    for (int i = 0; i < kChunk; ++i) {
+      const float4 qv = *reinterpret_cast<const float4 *>(&b.q[i][r0]);
+      pq[i] = fmaf(qv.w, S[3], fmaf(qv.z, S[2], fmaf(qv.y, S[1], qv.x * S[0])));
+    }
+    transpose_sum(pq, lane);
+    const float *R = b.rec;
+    const float rhs = R[REC_BETA + lane] * (b.v[lane][warp] - R[REC_A + lane] * pk[0]);
+    float d = 0.f;
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) d = fmaf(R[REC_TINV + j * kChunk + lane], __shfl_sync(0xffffffffu, rhs, j), d);
+    float o = R[REC_A + lane] * pq[0];
+    const float alast = R[REC_ALAST];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) S[r] *= alast;
+#pragma unroll 8
+    for (int j = 0; j < kChunk; ++j) {
+      const float dj = __shfl_sync(0xffffffffu, d, j);
+      o = fmaf(R[REC_MO + j * kChunk + lane], dj, o);
+      const float coef = R[REC_WS + j] * dj;
+      const float4 kv = *reinterpret_cast<const float4 *>(&b.k[j][r0]);
+      S[0] = fmaf(kv.x, coef, S[0]);
+      S[1] = fmaf(kv.y, coef, S[1]);
+      S[2] = fmaf(kv.z, coef, S[2]);
+      S[3] = fmaf(kv.w, coef, S[3]);
+    }
+    obuf[lane][warp] = o;
+    __syncthreads();
+    const int tok = ch * kChunk + tid;
+    if (tid < kChunk && tok < T) {
+      const float *ov = obuf[tid];
+      *reinterpret_cast<uint4 *>(core + ((long long)tok * HV + h) * DK + c0) =
+          make_uint4(pack2(ov[0], ov[1]), pack2(ov[2], ov[3]), pack2(ov[4], ov[5]), pack2(ov[6], ov[7]));
+    }
+    __syncthreads();
   }
   float *So = rec_out + (long long)h * DK * DK;
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    So[(long long)(r0 + r) * DK + c0] = S[r][0];
-    So[(long long)(r0 + r) * DK + c0 + 1] = S[r][1];
-  }
+  for (int r = 0; r < 4; ++r) So[(long long)(r0 + r) * DK + c] = S[r];
 }
 
 // Gated RMSNorm of token t, head h (HF Qwen3_5RMSNormGated): bf16(bf16(w * bf16(x r)) * silu(z)),
 // the sum of squares taken like the decode kernel's: per 16-value tile, then
 // ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)).
-__global__ void __launch_bounds__(128) gated_norm_kernel(const bf16 *core, const bf16 *z, const bf16 *w, bf16 *out,
-                                                         int HV, int DK, float eps) {
+__global__ void __launch_bounds__(128) gated_norm_kernel(const bf16 *core, const bf16 *z, int ld, const bf16 *w,
+                                                         bf16 *out, int HV, int DK, float eps) {
   const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const long long i = ((long long)t * HV + h) * DK + tid;
   __shared__ float part[8];
@@ -282,7 +446,7 @@ __global__ void __launch_bounds__(128) gated_norm_kernel(const bf16 *core, const
   const float tot = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
   const float r = rsqrtf(tot / (float)DK + eps);
   const float n = rbf(bf(w[tid]) * rbf(x * r));
-  const float zz = bf(z[i]);
+  const float zz = bf(z[(long long)t * ld + h * DK + tid]);
   out[i] = tobf(n * (zz / (1.f + expf(-zz))));
 }
 
@@ -290,7 +454,7 @@ __global__ void __launch_bounds__(128) gated_norm_kernel(const bf16 *core, const
 // fp32 angles, bf16 products and sum), as the decode kernel; one warp per (token, head). Heads
 // [0, HQ) are query heads (written to qatt [HQ, T, D]); [HQ, HQ + HKV) keys and
 // [HQ + HKV, HQ + 2 HKV) values, appended to the cache at position start + t.
-__global__ void attn_prep_kernel(const bf16 *qo, const bf16 *ko, const bf16 *vo, const bf16 *qnorm,
+__global__ void attn_prep_kernel(const bf16 *qo, const bf16 *ko, const bf16 *vo, int ld, const bf16 *qnorm,
                                  const bf16 *knorm, const float *inv_freq, bf16 *qatt, bf16 *kc, bf16 *vc,
                                  int HQ, int HKV, int D, int RD, int C, int T, long long start, float eps, int q35) {
   const int t = blockIdx.x, hh = blockIdx.y, lane = threadIdx.x, EPL = D / 32;
@@ -298,12 +462,12 @@ __global__ void attn_prep_kernel(const bf16 *qo, const bf16 *ko, const bf16 *vo,
   if (hh >= HQ + HKV) {
     const int kvh = hh - HQ - HKV;
     for (int d = lane; d < D; d += 32)
-      vc[((long long)kvh * C + pos) * D + d] = vo[((long long)t * HKV + kvh) * D + d];
+      vc[((long long)kvh * C + pos) * D + d] = vo[(long long)t * ld + kvh * D + d];
     return;
   }
   const bool isk = hh >= HQ;
   const int hd = isk ? hh - HQ : hh;
-  const bf16 *src = isk ? ko + ((long long)t * HKV + hd) * D : qo + ((long long)t * HQ + hd) * D * (q35 ? 2 : 1);
+  const bf16 *src = isk ? ko + (long long)t * ld + hd * D : qo + (long long)t * ld + hd * D * (q35 ? 2 : 1);
   const bf16 *nw = isk ? knorm : qnorm;
   float v[8], ss = 0.f;
   for (int e = 0; e < 8; ++e) {
@@ -336,12 +500,12 @@ __global__ void attn_prep_kernel(const bf16 *qo, const bf16 *ko, const bf16 *vo,
 
 // Attention output rows [T, HQ * D] for o_proj: Qwen3.5 multiplies by bf16(sigmoid(gate)) and
 // rounds (compiler/qwen35/adapters/attention.py:61-63); Qwen3 copies.
-__global__ void attn_out_kernel(const bf16 *oatt, const bf16 *qo, bf16 *out, int HQ, int D, int T, int q35) {
+__global__ void attn_out_kernel(const bf16 *oatt, const bf16 *qo, int ld, bf16 *out, int HQ, int D, int T, int q35) {
   const int t = blockIdx.x, h = blockIdx.y;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float y = bf(oatt[((long long)h * T + t) * D + d]);
     if (q35) {
-      const float g = bf(qo[((long long)t * HQ + h) * 2 * D + D + d]);
+      const float g = bf(qo[(long long)t * ld + h * 2 * D + D + d]);
       y = rbf(y * rbf(1.f / (1.f + expf(-g))));
     }
     out[((long long)t * HQ + h) * D + d] = tobf(y);
@@ -405,6 +569,13 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
                                              : (!s.k_cache || !s.v_cache))
       return xb::fail(XB_ERR_INVALID, "missing state in layer " + std::to_string(l));
   }
+  if (g.family == XB_FAMILY_QWEN35 && g.lin_head_dim != 128)
+    return xb::fail(XB_ERR_UNSUPPORTED, "prefill needs DeltaNet heads of dimension 128");
+  if (g.family == XB_FAMILY_QWEN35) {
+    const cudaError_t e = cudaFuncSetAttribute(delta_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)kScanSmem);
+    if (e != cudaSuccess) return xb::fail(XB_ERR_CUDA, std::string("prefill: ") + cudaGetErrorString(e));
+  }
   cudaStream_t st = (cudaStream_t)stream;
   char *ws = (char *)workspace;
   auto P = [&](size_t off) { return (bf16 *)(ws + off); };
@@ -426,45 +597,66 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
     cudaError_t e_ = cudaGetLastError();                                                             \
     if (e_ != cudaSuccess) return xb::fail(XB_ERR_CUDA, std::string("prefill launch: ") + cudaGetErrorString(e_)); \
   } while (0)
-  auto gemm = [&](int n, int k, const bf16 *xin, const void *w, bf16 *o) {
-    return xb_gemm_bf16(T, n, k, xin, w, o, stream);
+  const int NP = proj_width(g);
+  bf16 *proj = P(L.proj);
+  // One GEMM per group of projections that read the same rows when their weights are adjacent
+  // rows of one tensor (the reference's packed layout), else one GEMM per projection, each into
+  // its columns of the projection rows.
+  struct Part { const void *w; int rows; };
+  auto group = [&](const bf16 *xin, int k, std::initializer_list<Part> parts) -> int {
+    bool packed = true;
+    int rows = 0;
+    const Part *prev = nullptr;
+    for (const Part &p : parts) {
+      if (prev && (const char *)p.w != (const char *)prev->w + (size_t)prev->rows * k * 2) packed = false;
+      rows += p.rows;
+      prev = &p;
+    }
+    if (packed) return xb::gemm_bf16(T, rows, k, xin, parts.begin()->w, proj, NP, stream);
+    int col = 0;
+    for (const Part &p : parts) {
+      const int rc = xb::gemm_bf16(T, p.rows, k, xin, p.w, proj + col, NP, stream);
+      if (rc) return rc;
+      col += p.rows;
+    }
+    return XB_OK;
   };
-  const long long nH = (long long)T * H;
   const int eb = 296;  // elementwise grid: 2 CTAs per SM
   embed_kernel<<<T, 128, 0, st>>>(a->input_ids, (const bf16 *)model->w.embed, h, H, g.vocab, err);
+  XB_LAUNCHED();
+  add_rmsnorm_kernel<<<T, 256, 0, st>>>(h, nullptr, (const bf16 *)model->w.layers[0].input_norm, x, H, g.rms_eps,
+                                        q35, 0);
   XB_LAUNCHED();
   for (int l = 0; l < g.num_layers; ++l) {
     const XbLayerWeights &w = model->w.layers[l];
     const XbLayerState &s = a->layers[l];
-    rmsnorm_kernel<<<T, 256, 0, st>>>(h, (const bf16 *)w.input_norm, x, H, g.rms_eps, q35);
-    XB_LAUNCHED();
     if (g.layer_kind[l] == XB_LAYER_DELTANET) {
-      XB_TRY(gemm(CH, H, x, w.in_qkv, P(L.qkv)));
-      XB_TRY(gemm(HV * DK, H, x, w.in_z, P(L.z)));
-      XB_TRY(gemm(HV, H, x, w.in_b, P(L.bb)));
-      XB_TRY(gemm(HV, H, x, w.in_a, P(L.aa)));
+      const int HVD = HV * DK;
+      XB_TRY(group(x, H, {{w.in_qkv, CH}, {w.in_z, HVD}, {w.in_b, HV}, {w.in_a, HV}}));
+      const bf16 *qkv = proj, *z = proj + CH, *bb = proj + CH + HVD, *aa = proj + CH + HVD + HV;
       delta_prepare_kernel<<<dim3(T, HV), 256, 0, st>>>(
-          P(L.qkv), P(L.bb), P(L.aa), (const bf16 *)s.conv_in, (const bf16 *)w.conv_w, (const bf16 *)w.a_log,
-          (const bf16 *)w.dt_bias, F(L.qn), F(L.kn), F(L.vv), F(L.beta), F(L.decay), HK, HV, DK,
+          qkv, bb, aa, NP, (const bf16 *)s.conv_in, (const bf16 *)w.conv_w, (const bf16 *)w.a_log,
+          (const bf16 *)w.dt_bias, F(L.qn), F(L.kn), F(L.vv), F(L.beta), F(L.glog), HK, HV, DK,
           (float)(1.0 / std::sqrt((double)DK)));
       XB_LAUNCHED();
-      conv_state_kernel<<<(CH + 255) / 256, 256, 0, st>>>(P(L.qkv), (const bf16 *)s.conv_in, (bf16 *)s.conv_out, CH, T);
+      conv_state_kernel<<<(CH + 255) / 256, 256, 0, st>>>(qkv, NP, (const bf16 *)s.conv_in, (bf16 *)s.conv_out, CH, T);
       XB_LAUNCHED();
-      delta_scan_kernel<<<dim3(HV, DK / 16), 256, 0, st>>>(F(L.qn), F(L.kn), F(L.vv), F(L.beta), F(L.decay),
-                                                           (const float *)s.rec_in, (float *)s.rec_out,
-                                                           P(L.core), HV, DK, T);
+      delta_chunk_prep_kernel<<<dim3((T + kChunk - 1) / kChunk, HV), 256, 0, st>>>(F(L.qn), F(L.kn), F(L.glog),
+                                                                                F(L.beta), F(L.rec), HV, DK, T);
       XB_LAUNCHED();
-      gated_norm_kernel<<<dim3(T, HV), 128, 0, st>>>(P(L.core), P(L.z), (const bf16 *)w.gnorm, x2, HV, DK, g.rms_eps);
+      delta_chunk_scan_kernel<<<dim3(HV, DK / 8), 256, kScanSmem, st>>>(F(L.qn), F(L.kn), F(L.vv), F(L.rec),
+                                                                         (const float *)s.rec_in, (float *)s.rec_out,
+                                                                         P(L.core), HV, T);
       XB_LAUNCHED();
-      XB_TRY(gemm(H, HV * DK, x2, w.out_proj, out));
+      gated_norm_kernel<<<dim3(T, HV), 128, 0, st>>>(P(L.core), z, NP, (const bf16 *)w.gnorm, x2, HV, DK, g.rms_eps);
+      XB_LAUNCHED();
+      XB_TRY(xb::gemm_bf16(T, H, HVD, x2, w.out_proj, out, H, stream));
     } else {
       const int qrows = HQ * D * (q35 ? 2 : 1);
-      bf16 *qo = P(L.qkv), *ko = P(L.z), *vo = P(L.bb);
-      XB_TRY(gemm(qrows, H, x, w.q_proj, qo));
-      XB_TRY(gemm(HKV * D, H, x, w.k_proj, ko));
-      XB_TRY(gemm(HKV * D, H, x, w.v_proj, vo));
+      XB_TRY(group(x, H, {{w.q_proj, qrows}, {w.k_proj, HKV * D}, {w.v_proj, HKV * D}}));
+      const bf16 *qo = proj, *ko = proj + qrows, *vo = proj + qrows + HKV * D;
       attn_prep_kernel<<<dim3(T, HQ + 2 * HKV), 32, 0, st>>>(
-          qo, ko, vo, (const bf16 *)w.q_norm, (const bf16 *)w.k_norm, model->d_inv_freq, P(L.qatt),
+          qo, ko, vo, NP, (const bf16 *)w.q_norm, (const bf16 *)w.k_norm, model->d_inv_freq, P(L.qatt),
           (bf16 *)s.k_cache, (bf16 *)s.v_cache, HQ, HKV, D, g.rotary_dim, g.capacity, T, a->start_position,
           g.rms_eps, q35);
       XB_LAUNCHED();
@@ -483,26 +675,26 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
       at.length = (int32_t)(a->start_position + T);
       at.scale = (float)(1.0 / std::sqrt((double)D));
       XB_TRY(xb_prefix_attention(&at, stream));
-      attn_out_kernel<<<dim3(T, HQ), 128, 0, st>>>(P(L.oatt), qo, x2, HQ, D, T, q35);
+      attn_out_kernel<<<dim3(T, HQ), 128, 0, st>>>(P(L.oatt), qo, NP, x2, HQ, D, T, q35);
       XB_LAUNCHED();
-      XB_TRY(gemm(H, HQ * D, x2, w.o_proj, out));
+      XB_TRY(xb::gemm_bf16(T, H, HQ * D, x2, w.o_proj, out, H, stream));
     }
-    add_kernel<<<eb, 256, 0, st>>>(h, out, nH);
+    add_rmsnorm_kernel<<<T, 256, 0, st>>>(h, out, (const bf16 *)w.post_norm, x, H, g.rms_eps, q35, 0);
     XB_LAUNCHED();
-    rmsnorm_kernel<<<T, 256, 0, st>>>(h, (const bf16 *)w.post_norm, x, H, g.rms_eps, q35);
+    XB_TRY(group(x, H, {{w.gate, I}, {w.up, I}}));
+    silu_mul_kernel<<<eb, 256, 0, st>>>(proj, x2, I, NP, T);
     XB_LAUNCHED();
-    XB_TRY(gemm(I, H, x, w.gate, P(L.gate)));
-    XB_TRY(gemm(I, H, x, w.up, P(L.up)));
-    silu_mul_kernel<<<eb, 256, 0, st>>>(P(L.gate), P(L.up), x2, (long long)T * I);
-    XB_LAUNCHED();
-    XB_TRY(gemm(H, I, x2, w.down, out));
-    add_kernel<<<eb, 256, 0, st>>>(h, out, nH);
+    XB_TRY(xb::gemm_bf16(T, H, I, x2, w.down, out, H, stream));
+    if (l + 1 < g.num_layers) {
+      add_rmsnorm_kernel<<<T, 256, 0, st>>>(h, out, (const bf16 *)model->w.layers[l + 1].input_norm, x, H,
+                                            g.rms_eps, q35, 0);
+    } else {
+      // the last token only: residual add, final norm (ModelStep's last-token gather, model.py:178-183)
+      add_rmsnorm_kernel<<<1, 256, 0, st>>>(h, out, (const bf16 *)model->w.final_norm, P(L.xlast), H, g.rms_eps,
+                                            q35, T - 1);
+    }
     XB_LAUNCHED();
   }
-  // the last token: final norm, lm_head, argmax (ModelStep's last-token gather, model.py:178-183)
-  rmsnorm_kernel<<<1, 256, 0, st>>>(h + (long long)(T - 1) * H, (const bf16 *)model->w.final_norm, P(L.xlast), H,
-                                    g.rms_eps, q35);
-  XB_LAUNCHED();
   XB_TRY(xb_gemm_bf16(1, g.vocab, H, P(L.xlast), model->w.lm_head, a->logits, stream));
   if (a->next_token) {
     argmax_kernel<<<1, 1024, 0, st>>>((const bf16 *)a->logits, g.vocab, a->next_token);

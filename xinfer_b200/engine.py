@@ -26,6 +26,36 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
 
+def linear_groups(geometry):
+    """Per layer, the HF names of the projections that read the same input, in the order the
+    reference's pack_linears pass concatenates them (compiler/common/passes/pack_linears.py:22-142):
+    DeltaNet in_proj qkv | z | b | a, attention q | k | v, MLP gate | up."""
+    groups = []
+    for i in range(geometry.num_layers):
+        p = f"model.layers.{i}."
+        if geometry.is_delta(i):
+            groups.append([p + f"linear_attn.in_proj_{n}.weight" for n in ("qkv", "z", "b", "a")])
+        else:
+            groups.append([p + f"self_attn.{n}_proj.weight" for n in ("q", "k", "v")])
+        groups.append([p + f"mlp.{n}_proj.weight" for n in ("gate", "up")])
+    return groups
+
+
+def pack_linears(geometry, weights):
+    """A copy of `weights` whose projection groups (linear_groups) live as adjacent rows of one
+    tensor each, the layout of the reference's packed bundle; the HF names become views. The
+    prefill then runs one GEMM per group; the decode kernel streams the same rows either way."""
+    out = dict(weights)
+    for names in linear_groups(geometry):
+        parts = [weights[n] for n in names]
+        packed = torch.cat([t.reshape(t.shape[0], -1) for t in parts], dim=0)
+        row = 0
+        for n, t in zip(names, parts):
+            out[n] = packed[row:row + t.shape[0]].view(t.shape)
+            row += t.shape[0]
+    return out
+
+
 class Engine:
     """One model on one GPU: weight table, RoPE table, workspace."""
 
