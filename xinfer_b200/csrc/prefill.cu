@@ -27,6 +27,7 @@ namespace xbpre {
 using namespace xb;
 
 constexpr int kMaxTokens = 512;
+constexpr int kArgmaxBlocks = 296;  // CTAs of the logits argmax
 constexpr int kChunk = 32;  // tokens per step of the chunked gated delta rule
 // per (chunk, head): T^-1 and M (column-major, [j][i]), A_i, beta_i, A_32 / A_j, A_32
 constexpr int kRecFloats = 2 * kChunk * kChunk + 3 * kChunk + 32;
@@ -36,7 +37,7 @@ constexpr int kCtlBytes = 1024;
 enum { PERR_TOKEN = 4 };
 
 struct Layout {
-  size_t h, x, x2, out, proj, qn, kn, vv, beta, glog, rec, core, qatt, oatt, xlast, total;
+  size_t h, x, x2, out, proj, qn, kn, vv, rec, core, qatt, oatt, xlast, amax, total;
 };
 
 static int lin_channels(const XbGeometry &g) { return (2 * g.lin_key_heads + g.lin_value_heads) * g.lin_head_dim; }
@@ -67,13 +68,12 @@ static Layout layout(const XbGeometry &g, int T) {
   L.qn = take(vec);
   L.kn = take(vec);
   L.vv = take(vec);
-  L.beta = take(q35 ? (size_t)T * g.lin_value_heads * 4 : 256);
-  L.glog = take(q35 ? (size_t)T * g.lin_value_heads * 4 : 256);
   L.rec = take(q35 ? (size_t)((T + kChunk - 1) / kChunk) * g.lin_value_heads * kRecFloats * 4 : 256);
   L.core = take(q35 ? (size_t)T * HVD * 2 : 256);
   L.qatt = take((size_t)T * g.num_q_heads * g.head_dim * 2);
   L.oatt = take((size_t)T * g.num_q_heads * g.head_dim * 2);
   L.xlast = take((size_t)g.hidden * 2 + 16);
+  L.amax = take(kArgmaxBlocks * 8);
   L.total = off;
   return L;
 }
@@ -161,53 +161,6 @@ __global__ void silu_mul_kernel(const bf16 *proj, bf16 *act, int I, int ld, int 
   }
 }
 
-// DeltaNet preparation of token t, value head h (recurrent.py:32-58, 99-120 and the prepare step
-// of the long path, recurrent.py:127-189): width-4 causal conv over [old window, tokens] with fp32
-// FMAs in tap order, bf16, SiLU, bf16; q, k l2-normalised (q also scaled by dk^-0.5); beta =
-// bf16(sigmoid(b)); the log decay g = -exp(A_log) * softplus(a + dt_bias), softplus threshold 20.
-__global__ void __launch_bounds__(256) delta_prepare_kernel(
-    const bf16 *qkv, const bf16 *bb, const bf16 *aa, int ld, const bf16 *conv_in, const bf16 *conv_w,
-    const bf16 *a_log, const bf16 *dt_bias, float *qn, float *kn, float *vv, float *beta, float *glog,
-    int HK, int HV, int DK, float dk_scale) {
-  const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
-  const int kh = h / (HV / HK);
-  __shared__ float pn[8];
-  auto conv = [&](int ch) -> float {
-    float tot = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int s = t - 3 + j;
-      const float in = s < 0 ? bf(conv_in[(long long)ch * 4 + 4 + s]) : bf(qkv[(long long)s * ld + ch]);
-      tot = fmaf(in, bf(conv_w[(long long)ch * 4 + j]), tot);
-    }
-    const float v = rbf(tot);
-    return rbf(v * (1.f / (1.f + expf(-v))));
-  };
-  const int chq = tid < DK ? kh * DK + tid : (HK + kh) * DK + (tid - DK);
-  const float val = conv(chq);
-  const float sq = warp_sum(val * val);
-  if ((tid & 31) == 0) pn[tid >> 5] = sq;
-  float vch = 0.f;
-  if (tid < DK) vch = conv((2 * HK + h) * DK + tid);
-  __syncthreads();
-  const long long base = ((long long)t * HV + h) * DK;
-  if (tid < DK) {
-    const float qs = rsqrtf(pn[0] + pn[1] + pn[2] + pn[3] + 1e-6f);
-    qn[base + tid] = val * qs * dk_scale;
-    vv[base + tid] = vch;
-  } else {
-    const float ks = rsqrtf(pn[4] + pn[5] + pn[6] + pn[7] + 1e-6f);
-    kn[base + tid - DK] = val * ks;
-  }
-  if (tid == 0) {
-    const float b = bf(bb[(long long)t * ld + h]), a = bf(aa[(long long)t * ld + h]);
-    beta[(long long)t * HV + h] = rbf(1.f / (1.f + expf(-b)));
-    const float x = a + bf(dt_bias[h]);
-    const float sp = x > 20.f ? x : log1pf(expf(x));
-    glog[(long long)t * HV + h] = -expf(bf(a_log[h])) * sp;
-  }
-}
-
 // The conv window after the last token: the last four inputs of [old window, tokens] for every
 // channel (recurrent.py:43-52). Launched after every read of the old window, so in place is safe.
 __global__ void conv_state_kernel(const bf16 *qkv, int ld, const bf16 *conv_in, bf16 *conv_out, int CH, int T) {
@@ -236,32 +189,95 @@ __global__ void conv_state_kernel(const bf16 *qkv, int ld, const bf16 *conv_in, 
 enum { REC_TINV = 0, REC_MO = kChunk * kChunk, REC_A = 2 * kChunk * kChunk, REC_BETA = REC_A + kChunk,
        REC_WS = REC_BETA + kChunk, REC_ALAST = REC_WS + kChunk };
 
-// The chunk-local matrices of one (chunk, head), all from the keys, queries, gates and betas:
-// P, the Gram matrices k_i.k_j and q_i.k_j, T^-1 = (I + L)^-1 by forward substitution
-// (reference: _solve, chunked.py:17-44), M_ij = (A_i / A_j) q_i.k_j (j <= i).
-__global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float *qn, const float *kn, const float *glog,
-                                                               const float *beta, float *rec, int HV, int DK, int T) {
+// DeltaNet preparation and chunk-local matrices of one (chunk of 32 tokens, value head), one CTA:
+//  1. the prepare step (recurrent.py:32-58, 99-120; the long path's prepare_kernel,
+//     recurrent.py:127-189): width-4 causal conv over [old window, tokens] with fp32 FMAs in tap
+//     order, bf16, SiLU, bf16; q and k l2-normalised (q also scaled by dk^-0.5), the sum of squares
+//     taken as four 32-channel warp sums added in order; beta = bf16(sigmoid(b)); the log decay
+//     g = -exp(A_log) * softplus(a + dt_bias), softplus threshold 20. q, k, v go to global memory
+//     (fp32) for the scan;
+//  2. the chunk-local matrices (reference: _solve, chunked.py:17-44): P (in-order prefix sums of
+//     g), the Gram matrices k_i.k_j and q_i.k_j, T^-1 = (I + L)^-1 by forward substitution and
+//     M_ij = (A_i / A_j) q_i.k_j (j <= i), written as the chunk's record.
+__global__ void __launch_bounds__(256) delta_chunk_prepare_kernel(
+    const bf16 *qkv, const bf16 *bb, const bf16 *aa, int ld, const bf16 *conv_in, const bf16 *conv_w,
+    const bf16 *a_log, const bf16 *dt_bias, float *qn, float *kn, float *vv, float *rec, int HK, int HV, int T,
+    float dk_scale) {
+  constexpr int DK = 128;
   const int chunk = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int t0 = chunk * kChunk;
+  const int t0 = chunk * kChunk, kh = h / (HV / HK);
   __shared__ float ks[kChunk][129], qs[kChunk][129];
   __shared__ float P[kChunk], bt[kChunk], Lm[kChunk][kChunk + 1], Qm[kChunk][kChunk + 1];
-  for (int idx = tid; idx < kChunk * DK; idx += blockDim.x) {
-    const int t = idx / DK, d = idx % DK, tok = t0 + t;
-    const long long src = ((long long)tok * HV + h) * DK + d;
-    ks[t][d] = tok < T ? kn[src] : 0.f;
-    qs[t][d] = tok < T ? qn[src] : 0.f;
+  // 1a. conv + SiLU of the head's 384 channels (q, k of key head kh; v of value head h)
+  for (int lc = tid; lc < 3 * DK; lc += blockDim.x) {
+    const int part = lc / DK, d = lc % DK;
+    const int ch = (part == 0 ? kh : part == 1 ? HK + kh : 2 * HK + h) * DK + d;
+    float w[4], x[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[j] = bf(conv_w[(long long)ch * 4 + j]);
+#pragma unroll
+    for (int j = 1; j < 4; ++j) {
+      const int s = t0 - 4 + j;
+      x[j] = s < 0 ? bf(conv_in[(long long)ch * 4 + 4 + s]) : bf(qkv[(long long)s * ld + ch]);
+    }
+    for (int t = 0; t < kChunk; ++t) {
+      const int tok = t0 + t;
+      x[0] = x[1]; x[1] = x[2]; x[2] = x[3];
+      x[3] = tok < T ? bf(qkv[(long long)tok * ld + ch]) : 0.f;
+      float tot = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) tot = fmaf(x[j], w[j], tot);
+      const float v = rbf(tot);
+      const float y = tok < T ? rbf(v * (1.f / (1.f + expf(-v)))) : 0.f;
+      if (part == 0) qs[t][d] = y;
+      else if (part == 1) ks[t][d] = y;
+      else if (tok < T) vv[((long long)tok * HV + h) * DK + d] = y;
+    }
   }
+  // 1b. gates
   if (tid < kChunk) {
     const int tok = t0 + tid;
-    P[tid] = tok < T ? glog[(long long)tok * HV + h] : 0.f;
-    bt[tid] = tok < T ? beta[(long long)tok * HV + h] : 0.f;
+    float g = 0.f, b = 0.f;
+    if (tok < T) {
+      const float bv = bf(bb[(long long)tok * ld + h]), av = bf(aa[(long long)tok * ld + h]);
+      b = rbf(1.f / (1.f + expf(-bv)));
+      const float x = av + bf(dt_bias[h]);
+      const float sp = x > 20.f ? x : log1pf(expf(x));
+      g = -expf(bf(a_log[h])) * sp;
+    }
+    P[tid] = g;
+    bt[tid] = b;
+  }
+  __syncthreads();
+  // 1c. l2 norms, warp w takes tokens w, w + 8, w + 16, w + 24
+  for (int t = warp; t < kChunk; t += 8) {
+    const int tok = t0 + t;
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const float a = qs[t][g * 32 + lane], b = ks[t][g * 32 + lane];
+      sq += warp_sum(a * a);
+      sk += warp_sum(b * b);
+    }
+    const float rq = rsqrtf(sq + 1e-6f), rk = rsqrtf(sk + 1e-6f);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int d = g * 32 + lane;
+      const float q = qs[t][d] * rq * dk_scale, k = ks[t][d] * rk;
+      qs[t][d] = q;
+      ks[t][d] = k;
+      if (tok < T) {
+        qn[((long long)tok * HV + h) * DK + d] = q;
+        kn[((long long)tok * HV + h) * DK + d] = k;
+      }
+    }
   }
   __syncthreads();
   if (tid == 0) {
     float run = 0.f;
     for (int i = 0; i < kChunk; ++i) { run += P[i]; P[i] = run; }
   }
-  // Gram rows i = 4 warp .. 4 warp + 3 against key j = lane, summed over d in order
+  // 2. Gram rows i = 4 warp .. 4 warp + 3 against key j = lane, summed over d in order
   float ag[4] = {0.f, 0.f, 0.f, 0.f}, aq[4] = {0.f, 0.f, 0.f, 0.f};
   for (int d = 0; d < DK; ++d) {
     const float kj = ks[lane][d];
@@ -316,17 +332,19 @@ template <int N> __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
-// One CTA per (value head, 8 value columns), warp w owns column 8 blockIdx.y + w, lane l rows
-// 4l..4l + 3 of it. Per chunk (double-buffered in shared memory by cp.async): 32 key and query
-// projections of S_0 per lane, summed across the warp by a transposing butterfly (lane i ends with
-// token i's sums), then d = T^-1 rhs and o by broadcasts, then the state update.
+// One CTA per (value head, 16 value columns); warp w owns columns 16 blockIdx.y + 2w and + 1, lane l
+// rows 4l..4l + 3 of both (so every key and query row read from shared memory serves two
+// columns). Per chunk (double-buffered in shared memory by cp.async): 32 key and query
+// projections of S_0 per lane and column, summed across the warp by a transposing butterfly (lane i
+// ends with token i's sums), then d = T^-1 rhs and o by broadcasts, then the state update.
+constexpr int kScanCols = 16;
 struct ChunkBuf {
   float k[kChunk][128];
   float q[kChunk][128];
-  float v[kChunk][8];
+  float v[kChunk][kScanCols];
   float rec[kRecFloats];
 };
-constexpr size_t kScanSmem = 2 * sizeof(ChunkBuf) + kChunk * 8 * sizeof(float);
+constexpr size_t kScanSmem = 2 * sizeof(ChunkBuf) + kChunk * kScanCols * sizeof(float);
 
 __device__ __forceinline__ void transpose_sum(float (&v)[kChunk], int lane) {
 #pragma unroll
@@ -341,15 +359,32 @@ __device__ __forceinline__ void transpose_sum(float (&v)[kChunk], int lane) {
   }
 }
 
+// the 32 per-lane partial dot products of rows x_i (shared memory) with the lane's 4 state rows
+// of two columns, summed over the warp: lane i returns token i's sums
+__device__ __forceinline__ void project2(const float (*x)[128], int r0, const float (&S)[2][4], int lane,
+                                         float &out0, float &out1) {
+  float p0[kChunk], p1[kChunk];
+#pragma unroll
+  for (int i = 0; i < kChunk; ++i) {
+    const float4 xv = *reinterpret_cast<const float4 *>(&x[i][r0]);
+    p0[i] = fmaf(xv.w, S[0][3], fmaf(xv.z, S[0][2], fmaf(xv.y, S[0][1], xv.x * S[0][0])));
+    p1[i] = fmaf(xv.w, S[1][3], fmaf(xv.z, S[1][2], fmaf(xv.y, S[1][1], xv.x * S[1][0])));
+  }
+  transpose_sum(p0, lane);
+  transpose_sum(p1, lane);
+  out0 = p0[0];
+  out1 = p1[0];
+}
+
 __global__ void __launch_bounds__(256, 2) delta_chunk_scan_kernel(const float *qn, const float *kn, const float *vv,
-                                                               const float *rec, const float *rec_in, float *rec_out,
-                                                               bf16 *core, int HV, int T) {
+                                                                  const float *rec, const float *rec_in,
+                                                                  float *rec_out, bf16 *core, int HV, int T) {
   constexpr int DK = 128;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   ChunkBuf *buf = reinterpret_cast<ChunkBuf *>(smem_raw);
-  float(*obuf)[8] = reinterpret_cast<float(*)[8]>(smem_raw + 2 * sizeof(ChunkBuf));
-  const int h = blockIdx.x, c0 = blockIdx.y * 8, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int c = c0 + warp, r0 = lane * 4;
+  float(*obuf)[kScanCols] = reinterpret_cast<float(*)[kScanCols]>(smem_raw + 2 * sizeof(ChunkBuf));
+  const int h = blockIdx.x, c0 = blockIdx.y * kScanCols, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int cw = 2 * warp, r0 = lane * 4;
   const int nch = (T + kChunk - 1) / kChunk;
   auto issue = [&](int chunk, ChunkBuf &b) {
     const int t0 = chunk * kChunk;
@@ -359,18 +394,20 @@ __global__ void __launch_bounds__(256, 2) delta_chunk_scan_kernel(const float *q
       cp_async16(&b.k[t][d4 * 4], kn + src, tok < T);
       cp_async16(&b.q[t][d4 * 4], qn + src, tok < T);
     }
-    if (tid < kChunk * 2) {
-      const int t = tid >> 1, half = tid & 1, tok = t0 + t;
-      cp_async16(&b.v[t][half * 4], vv + ((long long)min(tok, T - 1) * HV + h) * DK + c0 + half * 4, tok < T);
+    if (tid < kChunk * kScanCols / 4) {
+      const int t = tid / (kScanCols / 4), part = tid % (kScanCols / 4), tok = t0 + t;
+      cp_async16(&b.v[t][part * 4], vv + ((long long)min(tok, T - 1) * HV + h) * DK + c0 + part * 4, tok < T);
     }
     const float *src = rec + ((long long)chunk * HV + h) * kRecFloats;
     for (int idx = tid; idx < kRecFloats / 4; idx += 256) cp_async16(&b.rec[idx * 4], src + idx * 4, true);
     cp_async_commit();
   };
   const float *Si = rec_in + (long long)h * DK * DK;
-  float S[4];
+  float S[2][4];
 #pragma unroll
-  for (int r = 0; r < 4; ++r) S[r] = Si[(long long)(r0 + r) * DK + c];
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) S[c][r] = Si[(long long)(r0 + r) * DK + c0 + cw + c];
   issue(0, buf[0]);
   for (int ch = 0; ch < nch; ++ch) {
     if (ch + 1 < nch) {
@@ -381,52 +418,61 @@ __global__ void __launch_bounds__(256, 2) delta_chunk_scan_kernel(const float *q
     }
     __syncthreads();
     const ChunkBuf &b = buf[ch & 1];
-    float pk[kChunk], pq[kChunk];
-#pragma unroll
-    for (int i = 0; i < kChunk; ++i) {
-      const float4 kv = *reinterpret_cast<const float4 *>(&b.k[i][r0]);
-      pk[i] = fmaf(kv.w, S[3], fmaf(kv.z, S[2], fmaf(kv.y, S[1], kv.x * S[0])));
-    }
-    transpose_sum(pk, lane);
-#pragma unroll
-    for (int i = 0; i < kChunk; ++i) {
-      const float4 qv = *reinterpret_cast<const float4 *>(&b.q[i][r0]);
-      pq[i] = fmaf(qv.w, S[3], fmaf(qv.z, S[2], fmaf(qv.y, S[1], qv.x * S[0])));
-    }
-    transpose_sum(pq, lane);
     const float *R = b.rec;
-    const float rhs = R[REC_BETA + lane] * (b.v[lane][warp] - R[REC_A + lane] * pk[0]);
-    float d = 0.f;
+    float pk0, pk1, pq0, pq1;
+    project2(b.k, r0, S, lane, pk0, pk1);
+    project2(b.q, r0, S, lane, pq0, pq1);
+    const float A = R[REC_A + lane], beta = R[REC_BETA + lane];
+    const float rhs0 = beta * (b.v[lane][cw] - A * pk0), rhs1 = beta * (b.v[lane][cw + 1] - A * pk1);
+    float d0 = 0.f, d1 = 0.f;
 #pragma unroll
-    for (int j = 0; j < kChunk; ++j) d = fmaf(R[REC_TINV + j * kChunk + lane], __shfl_sync(0xffffffffu, rhs, j), d);
-    float o = R[REC_A + lane] * pq[0];
+    for (int j = 0; j < kChunk; ++j) {
+      const float t = R[REC_TINV + j * kChunk + lane];
+      d0 = fmaf(t, __shfl_sync(0xffffffffu, rhs0, j), d0);
+      d1 = fmaf(t, __shfl_sync(0xffffffffu, rhs1, j), d1);
+    }
+    float o0 = A * pq0, o1 = A * pq1;
     const float alast = R[REC_ALAST];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) S[r] *= alast;
+    for (int r = 0; r < 4; ++r) {
+      S[0][r] *= alast;
+      S[1][r] *= alast;
+    }
 #pragma unroll 8
     for (int j = 0; j < kChunk; ++j) {
-      const float dj = __shfl_sync(0xffffffffu, d, j);
-      o = fmaf(R[REC_MO + j * kChunk + lane], dj, o);
-      const float coef = R[REC_WS + j] * dj;
+      const float dj0 = __shfl_sync(0xffffffffu, d0, j), dj1 = __shfl_sync(0xffffffffu, d1, j);
+      const float m = R[REC_MO + j * kChunk + lane], ws = R[REC_WS + j];
+      o0 = fmaf(m, dj0, o0);
+      o1 = fmaf(m, dj1, o1);
+      const float e0 = ws * dj0, e1 = ws * dj1;
       const float4 kv = *reinterpret_cast<const float4 *>(&b.k[j][r0]);
-      S[0] = fmaf(kv.x, coef, S[0]);
-      S[1] = fmaf(kv.y, coef, S[1]);
-      S[2] = fmaf(kv.z, coef, S[2]);
-      S[3] = fmaf(kv.w, coef, S[3]);
+      S[0][0] = fmaf(kv.x, e0, S[0][0]);
+      S[0][1] = fmaf(kv.y, e0, S[0][1]);
+      S[0][2] = fmaf(kv.z, e0, S[0][2]);
+      S[0][3] = fmaf(kv.w, e0, S[0][3]);
+      S[1][0] = fmaf(kv.x, e1, S[1][0]);
+      S[1][1] = fmaf(kv.y, e1, S[1][1]);
+      S[1][2] = fmaf(kv.z, e1, S[1][2]);
+      S[1][3] = fmaf(kv.w, e1, S[1][3]);
     }
-    obuf[lane][warp] = o;
+    obuf[lane][cw] = o0;
+    obuf[lane][cw + 1] = o1;
     __syncthreads();
-    const int tok = ch * kChunk + tid;
-    if (tid < kChunk && tok < T) {
-      const float *ov = obuf[tid];
-      *reinterpret_cast<uint4 *>(core + ((long long)tok * HV + h) * DK + c0) =
-          make_uint4(pack2(ov[0], ov[1]), pack2(ov[2], ov[3]), pack2(ov[4], ov[5]), pack2(ov[6], ov[7]));
+    if (tid < kChunk * 2) {
+      const int t = tid >> 1, half = tid & 1, tok = ch * kChunk + t;
+      if (tok < T) {
+        const float *ov = &obuf[t][half * 8];
+        *reinterpret_cast<uint4 *>(core + ((long long)tok * HV + h) * DK + c0 + half * 8) =
+            make_uint4(pack2(ov[0], ov[1]), pack2(ov[2], ov[3]), pack2(ov[4], ov[5]), pack2(ov[6], ov[7]));
+      }
     }
     __syncthreads();
   }
   float *So = rec_out + (long long)h * DK * DK;
 #pragma unroll
-  for (int r = 0; r < 4; ++r) So[(long long)(r0 + r) * DK + c] = S[r];
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) So[(long long)(r0 + r) * DK + c0 + cw + c] = S[c][r];
 }
 
 // Gated RMSNorm of token t, head h (HF Qwen3_5RMSNormGated): bf16(bf16(w * bf16(x r)) * silu(z)),
@@ -512,14 +558,10 @@ __global__ void attn_out_kernel(const bf16 *oatt, const bf16 *qo, int ld, bf16 *
   }
 }
 
-// torch.argmax of one bf16 row: first maximal index, NaN counts as the maximum.
-__global__ void __launch_bounds__(1024) argmax_kernel(const bf16 *row, int n, int64_t *token) {
-  float bv = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = bf(row[i]);
-    if (argmax_better(v, i, bv, bi)) { bv = v; bi = i; }
-  }
+// torch.argmax of one bf16 row (first maximal index, NaN counts as the maximum) in two launches:
+// each CTA reduces a contiguous range to one candidate, then one CTA reduces the candidates in
+// range order.
+__device__ __forceinline__ void block_argmax(float &bv, int &bi) {
   __shared__ float sv[32];
   __shared__ int si[32];
 #pragma unroll
@@ -530,11 +572,30 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const bf16 *row, int n, in
   }
   if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0)
     for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
       if (argmax_better(sv[w], si[w], bv, bi)) { bv = sv[w]; bi = si[w]; }
-    *token = bi;
+}
+
+__global__ void __launch_bounds__(256) argmax_partial_kernel(const bf16 *row, int n, float *cand_v, int *cand_i) {
+  const int per = (n + gridDim.x - 1) / gridDim.x, lo = blockIdx.x * per, hi = min(n, lo + per);
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const float v = bf(row[i]);
+    if (argmax_better(v, i, bv, bi)) { bv = v; bi = i; }
   }
+  block_argmax(bv, bi);
+  if (threadIdx.x == 0) { cand_v[blockIdx.x] = bv; cand_i[blockIdx.x] = bi; }
+}
+
+__global__ void __launch_bounds__(256) argmax_final_kernel(const float *cand_v, const int *cand_i, int n, int64_t *token) {
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    if (argmax_better(cand_v[i], cand_i[i], bv, bi)) { bv = cand_v[i]; bi = cand_i[i]; }
+  block_argmax(bv, bi);
+  if (threadIdx.x == 0) *token = bi;
 }
 
 } // namespace xbpre
@@ -634,19 +695,14 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
       const int HVD = HV * DK;
       XB_TRY(group(x, H, {{w.in_qkv, CH}, {w.in_z, HVD}, {w.in_b, HV}, {w.in_a, HV}}));
       const bf16 *qkv = proj, *z = proj + CH, *bb = proj + CH + HVD, *aa = proj + CH + HVD + HV;
-      delta_prepare_kernel<<<dim3(T, HV), 256, 0, st>>>(
+      delta_chunk_prepare_kernel<<<dim3((T + kChunk - 1) / kChunk, HV), 256, 0, st>>>(
           qkv, bb, aa, NP, (const bf16 *)s.conv_in, (const bf16 *)w.conv_w, (const bf16 *)w.a_log,
-          (const bf16 *)w.dt_bias, F(L.qn), F(L.kn), F(L.vv), F(L.beta), F(L.glog), HK, HV, DK,
-          (float)(1.0 / std::sqrt((double)DK)));
+          (const bf16 *)w.dt_bias, F(L.qn), F(L.kn), F(L.vv), F(L.rec), HK, HV, T, (float)(1.0 / std::sqrt((double)DK)));
       XB_LAUNCHED();
       conv_state_kernel<<<(CH + 255) / 256, 256, 0, st>>>(qkv, NP, (const bf16 *)s.conv_in, (bf16 *)s.conv_out, CH, T);
       XB_LAUNCHED();
-      delta_chunk_prep_kernel<<<dim3((T + kChunk - 1) / kChunk, HV), 256, 0, st>>>(F(L.qn), F(L.kn), F(L.glog),
-                                                                                F(L.beta), F(L.rec), HV, DK, T);
-      XB_LAUNCHED();
-      delta_chunk_scan_kernel<<<dim3(HV, DK / 8), 256, kScanSmem, st>>>(F(L.qn), F(L.kn), F(L.vv), F(L.rec),
-                                                                         (const float *)s.rec_in, (float *)s.rec_out,
-                                                                         P(L.core), HV, T);
+      delta_chunk_scan_kernel<<<dim3(HV, DK / kScanCols), 256, kScanSmem, st>>>(
+          F(L.qn), F(L.kn), F(L.vv), F(L.rec), (const float *)s.rec_in, (float *)s.rec_out, P(L.core), HV, T);
       XB_LAUNCHED();
       gated_norm_kernel<<<dim3(T, HV), 128, 0, st>>>(P(L.core), z, NP, (const bf16 *)w.gnorm, x2, HV, DK, g.rms_eps);
       XB_LAUNCHED();
@@ -697,7 +753,11 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
   }
   XB_TRY(xb_gemm_bf16(1, g.vocab, H, P(L.xlast), model->w.lm_head, a->logits, stream));
   if (a->next_token) {
-    argmax_kernel<<<1, 1024, 0, st>>>((const bf16 *)a->logits, g.vocab, a->next_token);
+    argmax_partial_kernel<<<kArgmaxBlocks, 256, 0, st>>>((const bf16 *)a->logits, g.vocab, F(L.amax),
+                                                         (int *)(ws + L.amax) + kArgmaxBlocks);
+    XB_LAUNCHED();
+    argmax_final_kernel<<<1, 256, 0, st>>>(F(L.amax), (const int *)(ws + L.amax) + kArgmaxBlocks, kArgmaxBlocks,
+                                           a->next_token);
     XB_LAUNCHED();
   }
 #undef XB_TRY
