@@ -2,8 +2,9 @@
 
     python -m xinfer_b200.build [--force]
 
-  * xinfer_b200/libxinfer_b200.so from xinfer_b200/csrc/*.cu with nvcc for sm_100a: the plain C
-    ABI of include/xinfer_b200.h, linked against the CUDA runtime only (no torch);
+  * xinfer_b200/libxinfer_b200.so from xinfer_b200/csrc/*.cu with nvcc for sm_100a (one object per
+    translation unit, compiled in parallel): the plain C ABI of include/xinfer_b200.h, linked
+    against the CUDA runtime only (no torch);
   * xinfer_b200/libxinfer_b200_ops.so from xinfer_b200/csrc/torch_ops.cpp with the host C++
     compiler: the xinfer::qwen3_decode_step / qwen35_decode_step torch operators and their
     AOTInductor C shims, linked against libtorch and libxinfer_b200.so (found next to it).
@@ -23,6 +24,7 @@ INCLUDE = ROOT / "include"
 OUT = PKG / "libxinfer_b200.so"
 OPS_SRC = CSRC / "torch_ops.cpp"
 OPS_OUT = PKG / "libxinfer_b200_ops.so"
+BUILD_DIR = PKG / "_build"  # object files (not committed)
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -36,8 +38,7 @@ def cutlass_includes():
     if not all((p / "cutlass").is_dir() for p in inc):
         raise RuntimeError(f"CUTLASS headers not found under {root}")
     return [f"-I{p}" for p in inc]
-FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-         "--expt-relaxed-constexpr", "-Xptxas", "-v"]
+FLAGS_CU = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr", "-Xptxas", "-v"]
 
 
 def nvcc():
@@ -92,17 +93,40 @@ def up_to_date():
     return all(p.stat().st_mtime <= t for p in sources() + headers())
 
 
-def build(force=False, verbose=False):
-    if not force and up_to_date():
-        return OUT
-    cmd = [nvcc(), *ARCH, *FLAGS, f"-I{INCLUDE}", f"-I{CSRC}", *cutlass_includes(), "-o", str(OUT) + ".tmp",
-           *map(str, sources())]
+def _compile(src, obj, force):
+    """One translation unit to an object file (skipped when the object is newer than it and every
+    header); returns the ptxas report."""
+    newest = max([src.stat().st_mtime] + [h.stat().st_mtime for h in headers()])
+    if not force and obj.exists() and obj.stat().st_mtime >= newest:
+        return ""
+    cmd = [nvcc(), *ARCH, *FLAGS_CU, f"-I{INCLUDE}", f"-I{CSRC}", *cutlass_includes(), "-c", "-o", str(obj) + ".tmp",
+           str(src)]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     log = proc.stdout + proc.stderr
     if proc.returncode != 0:
         raise RuntimeError(f"nvcc failed:\n{' '.join(cmd)}\n{log}")
+    os.replace(str(obj) + ".tmp", obj)
+    return f"== {src.name}\n{log}"
+
+
+def build(force=False, verbose=False):
+    if not force and up_to_date():
+        return OUT
+    from concurrent.futures import ThreadPoolExecutor
+
+    BUILD_DIR.mkdir(exist_ok=True)
+    srcs = sources()
+    objs = [BUILD_DIR / (s.stem + ".o") for s in srcs]
+    with ThreadPoolExecutor(max_workers=max(1, min(len(srcs), os.cpu_count() or 1))) as pool:
+        logs = list(pool.map(lambda so: _compile(so[0], so[1], force), zip(srcs, objs)))
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(OUT) + ".tmp", *map(str, objs)]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(f"nvcc link failed:\n{' '.join(cmd)}\n{proc.stdout}{proc.stderr}")
     os.replace(str(OUT) + ".tmp", OUT)
-    (PKG / "build_ptxas.log").write_text(log)
+    log = "".join(logs)
+    if log:
+        (PKG / "build_ptxas.log").write_text(log)
     if verbose:
         print(log)
     return OUT

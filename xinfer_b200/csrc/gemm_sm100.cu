@@ -1,76 +1,20 @@
-// Dense bf16 GEMM of the prefill projections on sm_100a tensor cores:
-//   out[M, N] = x[M, K] . W[N, K]^T      (x: M tokens of activations, W: an HF [out, in] weight)
-// with fp32 accumulation and one rounding to bf16, the rounding of the reference's cuBLAS
-// linears as lowered by Inductor (a bf16 nn.Linear).
-//
-// The kernel is CUTLASS's SM100 warp-specialised GEMM (cute/CUTLASS 4.x templates): TMA tile
-// loads of A and B into shared memory (one CTA per tile, cluster 1x1x1, so no multicast), MMAs
-// issued by a single thread with tcgen05.mma into a TMEM accumulator, a TMA-store epilogue.
-// Tiles of 128 (tokens) x 128 (weight rows) x 64.
-#include "cutlass/cutlass.h"
-#include "cute/tensor.hpp"
-#include "cutlass/epilogue/collective/collective_builder.hpp"
-#include "cutlass/gemm/collective/collective_builder.hpp"
-#include "cutlass/gemm/device/gemm_universal_adapter.h"
-#include "cutlass/gemm/kernel/gemm_universal.hpp"
-#include "cutlass/util/packed_stride.hpp"
-
-#include <cstring>
-#include <mutex>
-#include <string>
-#include <unordered_map>
-
-#include "xb_host.h"
-
+// Dense bf16 GEMM of the prefill projections (out[M, N] = x[M, K] . W[N, K]^T, fp32 accumulation,
+// one rounding to bf16): the choice among the sm_100a tensor-core configurations of
+// gemm_sm100.cuh by shape, and a plain kernel for outputs the tensor-core epilogue cannot store
+// (N or the row stride not a multiple of 8 elements).
+#include "gemm_sm100.cuh"
 
 namespace xbgemm {
-using namespace cute;
-using ElementA = cutlass::bfloat16_t;
-using LayoutA = cutlass::layout::RowMajor;     // x [M, K]
-using ElementB = cutlass::bfloat16_t;
-using LayoutB = cutlass::layout::ColumnMajor;  // W [N, K] read as a K x N column-major matrix
-using ElementD = cutlass::bfloat16_t;
-using LayoutD = cutlass::layout::RowMajor;     // out [M, N]
-using Accumulator = float;
-constexpr int kAlign = 8;  // 16-byte rows
-using TileShape = Shape<_128, _128, _64>;
-using ClusterShape = Shape<_1, _1, _1>;
-using Epilogue = typename cutlass::epilogue::collective::CollectiveBuilder<
-    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, TileShape, ClusterShape,
-    cutlass::epilogue::collective::EpilogueTileAuto, Accumulator, Accumulator, void, LayoutD, kAlign,
-    ElementD, LayoutD, kAlign, cutlass::epilogue::TmaWarpSpecialized1Sm>::CollectiveOp;
-using Mainloop = typename cutlass::gemm::collective::CollectiveBuilder<
-    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, ElementA, LayoutA, kAlign, ElementB, LayoutB,
-    kAlign, Accumulator, TileShape, ClusterShape,
-    cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(sizeof(typename Epilogue::SharedStorage))>,
-    cutlass::gemm::KernelTmaWarpSpecialized1SmSm100>::CollectiveOp;
-using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue>;
-using Gemm = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
+int run_narrow(int m, int n, int k, const void *x, const void *w, void *out, long long ldo, cudaStream_t st,
+               int device) {
+  return run<Narrow>(m, n, k, x, w, out, ldo, st, device);
+}
+int run_rows(int m, int n, int k, const void *x, const void *w, void *out, long long ldo, cudaStream_t st, int device) {
+  return run<Rows>(m, n, k, x, w, out, ldo, st, device);
+}
 } // namespace xbgemm
 
 namespace {
-// Launch parameters (TMA descriptors included) of every (shape, operands, device) seen: a prefill
-// chunk runs the same GEMMs on the same buffers again and again, and building the descriptors is
-// host work comparable to the kernel itself at these sizes.
-struct PlanKey {
-  int m, n, k, device;
-  long long ldo;
-  const void *x, *w;
-  void *out;
-  bool operator==(const PlanKey &o) const { return std::memcmp(this, &o, sizeof(PlanKey)) == 0; }
-};
-struct PlanHash {
-  size_t operator()(const PlanKey &p) const {
-    size_t h = 1469598103934665603ull;
-    const unsigned char *b = reinterpret_cast<const unsigned char *>(&p);
-    for (size_t i = 0; i < sizeof(PlanKey); ++i) h = (h ^ b[i]) * 1099511628211ull;
-    return h;
-  }
-};
-constexpr size_t kMaxPlans = 4096;
-std::mutex plan_mu;
-std::unordered_map<PlanKey, xbgemm::Gemm::Params, PlanHash> plans;
-
 // out[m, n] = x[m, :] . w[n, :] for shapes the tensor-core kernel cannot take (n not a multiple
 // of 8): one warp per output element, fp32 sum, one rounding.
 __global__ void gemm_rows_kernel(int m, int n, int k, const __nv_bfloat16 *x, const __nv_bfloat16 *w,
@@ -115,37 +59,10 @@ int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, 
   }
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return xb::fail(XB_ERR_CUDA, "GEMM: no current device");
-  const PlanKey key{m, n, k, device, ldo, x, w, out};
-  {
-    std::lock_guard<std::mutex> lock(plan_mu);
-    auto it = plans.find(key);
-    if (it != plans.end()) {
-      if (Gemm::run(it->second, st) != cutlass::Status::kSuccess) return xb::fail(XB_ERR_CUDA, "GEMM launch failed");
-      return XB_OK;
-    }
-  }
-  using SA = typename Kernel::StrideA;
-  using SB = typename Kernel::StrideB;
-  using SD = typename Kernel::StrideD;
-  const SA sa = cutlass::make_cute_packed_stride(SA{}, make_shape(m, k, 1));
-  const SB sb = cutlass::make_cute_packed_stride(SB{}, make_shape(n, k, 1));
-  SD sd = cutlass::make_cute_packed_stride(SD{}, make_shape(m, n, 1));
-  cute::get<0>(sd) = ldo;
-  typename Gemm::Arguments args{cutlass::gemm::GemmUniversalMode::kGemm,
-                                {m, n, k, 1},
-                                {static_cast<const ElementA *>(x), sa, static_cast<const ElementB *>(w), sb},
-                                {{1.f, 0.f}, nullptr, sd, static_cast<ElementD *>(out), sd}};
-  Gemm gemm;
-  if (gemm.can_implement(args) != cutlass::Status::kSuccess)
-    return xb::fail(XB_ERR_UNSUPPORTED, "GEMM shape not supported by the sm_100 kernel");
-  if (Gemm::get_workspace_size(args) != 0) return xb::fail(XB_ERR_UNSUPPORTED, "GEMM needs a workspace");
-  if (gemm.initialize(args, nullptr, st) != cutlass::Status::kSuccess)
-    return xb::fail(XB_ERR_CUDA, "GEMM initialisation failed");
-  if (gemm.run(st) != cutlass::Status::kSuccess) return xb::fail(XB_ERR_CUDA, "GEMM launch failed");
-  std::lock_guard<std::mutex> lock(plan_mu);
-  if (plans.size() >= kMaxPlans) plans.clear();
-  plans.emplace(key, gemm.params());
-  return XB_OK;
+  // measured on B200 over the prefill shapes of Qwen3.5-0.8B / 4B at 512 tokens
+  if (m <= 64) return run_rows(m, n, k, x, w, out, ldo, st, device);
+  if (n < 2048) return run_narrow(m, n, k, x, w, out, ldo, st, device);
+  return run_wide(m, n, k, x, w, out, ldo, st, device);
 }
 
 extern "C" int xb_gemm_bf16(int32_t m, int32_t n, int32_t k, const void *x, const void *w, void *out,

@@ -212,26 +212,30 @@ __global__ void __launch_bounds__(256) delta_chunk_prepare_kernel(
   for (int lc = tid; lc < 3 * DK; lc += blockDim.x) {
     const int part = lc / DK, d = lc % DK;
     const int ch = (part == 0 ? kh : part == 1 ? HK + kh : 2 * HK + h) * DK + d;
-    float w[4], x[4];
+    float w[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) w[j] = bf(conv_w[(long long)ch * 4 + j]);
+    // eight tokens at a time: their eleven window inputs are loaded before the first use
+#pragma unroll 1
+    for (int t8 = 0; t8 < kChunk; t8 += 8) {
+      float x[11];
 #pragma unroll
-    for (int j = 1; j < 4; ++j) {
-      const int s = t0 - 4 + j;
-      x[j] = s < 0 ? bf(conv_in[(long long)ch * 4 + 4 + s]) : bf(qkv[(long long)s * ld + ch]);
-    }
-    for (int t = 0; t < kChunk; ++t) {
-      const int tok = t0 + t;
-      x[0] = x[1]; x[1] = x[2]; x[2] = x[3];
-      x[3] = tok < T ? bf(qkv[(long long)tok * ld + ch]) : 0.f;
-      float tot = 0.f;
+      for (int j = 0; j < 11; ++j) {
+        const int s = t0 + t8 - 3 + j;
+        x[j] = s < 0 ? bf(conv_in[(long long)ch * 4 + 4 + s]) : s < T ? bf(qkv[(long long)s * ld + ch]) : 0.f;
+      }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) tot = fmaf(x[j], w[j], tot);
-      const float v = rbf(tot);
-      const float y = tok < T ? rbf(v * (1.f / (1.f + expf(-v)))) : 0.f;
-      if (part == 0) qs[t][d] = y;
-      else if (part == 1) ks[t][d] = y;
-      else if (tok < T) vv[((long long)tok * HV + h) * DK + d] = y;
+      for (int u = 0; u < 8; ++u) {
+        const int t = t8 + u, tok = t0 + t;
+        float tot = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tot = fmaf(x[u + j], w[j], tot);
+        const float v = rbf(tot);
+        const float y = tok < T ? rbf(v * (1.f / (1.f + expf(-v)))) : 0.f;
+        if (part == 0) qs[t][d] = y;
+        else if (part == 1) ks[t][d] = y;
+        else if (tok < T) vv[((long long)tok * HV + h) * DK + d] = y;
+      }
     }
   }
   // 1b. gates
