@@ -37,7 +37,7 @@ constexpr int kCtlBytes = 1024;
 enum { PERR_TOKEN = 4 };
 
 struct Layout {
-  size_t h, x, x2, out, proj, qn, kn, vv, rec, core, qatt, oatt, xlast, amax, total;
+  size_t h, x, x2, out, proj, qn, kn, vv, beta, glog, rec, core, qatt, oatt, xlast, amax, total;
 };
 
 static int lin_channels(const XbGeometry &g) { return (2 * g.lin_key_heads + g.lin_value_heads) * g.lin_head_dim; }
@@ -68,6 +68,8 @@ static Layout layout(const XbGeometry &g, int T) {
   L.qn = take(vec);
   L.kn = take(vec);
   L.vv = take(vec);
+  L.beta = take(q35 ? (size_t)T * g.lin_value_heads * 4 : 256);
+  L.glog = take(q35 ? (size_t)T * g.lin_value_heads * 4 : 256);
   L.rec = take(q35 ? (size_t)((T + kChunk - 1) / kChunk) * g.lin_value_heads * kRecFloats * 4 : 256);
   L.core = take(q35 ? (size_t)T * HVD * 2 : 256);
   L.qatt = take((size_t)T * g.num_q_heads * g.head_dim * 2);
@@ -189,128 +191,130 @@ __global__ void conv_state_kernel(const bf16 *qkv, int ld, const bf16 *conv_in, 
 enum { REC_TINV = 0, REC_MO = kChunk * kChunk, REC_A = 2 * kChunk * kChunk, REC_BETA = REC_A + kChunk,
        REC_WS = REC_BETA + kChunk, REC_ALAST = REC_WS + kChunk };
 
-// DeltaNet preparation and chunk-local matrices of one (chunk of 32 tokens, value head), one CTA:
-//  1. the prepare step (recurrent.py:32-58, 99-120; the long path's prepare_kernel,
-//     recurrent.py:127-189): width-4 causal conv over [old window, tokens] with fp32 FMAs in tap
-//     order, bf16, SiLU, bf16; q and k l2-normalised (q also scaled by dk^-0.5), the sum of squares
-//     taken as four 32-channel warp sums added in order; beta = bf16(sigmoid(b)); the log decay
-//     g = -exp(A_log) * softplus(a + dt_bias), softplus threshold 20. q, k, v go to global memory
-//     (fp32) for the scan;
-//  2. the chunk-local matrices (reference: _solve, chunked.py:17-44): P (in-order prefix sums of
-//     g), the Gram matrices k_i.k_j and q_i.k_j, T^-1 = (I + L)^-1 by forward substitution and
-//     M_ij = (A_i / A_j) q_i.k_j (j <= i), written as the chunk's record.
-__global__ void __launch_bounds__(256) delta_chunk_prepare_kernel(
+// DeltaNet preparation (recurrent.py:32-58, 99-120; the long path's prepare_kernel,
+// recurrent.py:127-189), one warp per (token, head part): part p < HK is query head p, p < 2 HK
+// key head p - HK, else value head p - 2 HK. Lane l takes channels 4l..4l + 3 of the part: width-4
+// causal conv over [old window, tokens] with fp32 FMAs in tap order, bf16, SiLU, bf16; q and k
+// l2-normalised (q also scaled by dk^-0.5). The value-head warps also make beta = bf16(sigmoid(b))
+// and the log decay g = -exp(A_log) * softplus(a + dt_bias), softplus threshold 20. Outputs fp32:
+// q, k per key head [T, HK, 128], v per value head [T, HV, 128], beta and g [T, HV].
+__global__ void __launch_bounds__(256) delta_prepare_kernel(
     const bf16 *qkv, const bf16 *bb, const bf16 *aa, int ld, const bf16 *conv_in, const bf16 *conv_w,
-    const bf16 *a_log, const bf16 *dt_bias, float *qn, float *kn, float *vv, float *rec, int HK, int HV, int T,
-    float dk_scale) {
+    const bf16 *a_log, const bf16 *dt_bias, float *qn, float *kn, float *vv, float *beta, float *glog, int HK,
+    int HV, int T, float dk_scale) {
   constexpr int DK = 128;
+  const int parts = 2 * HK + HV, lane = threadIdx.x & 31;
+  const long long unit = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (unit >= (long long)T * parts) return;
+  const int t = (int)(unit / parts), p = (int)(unit % parts);
+  const int ch0 = p * DK + lane * 4;
+  float w[4][4], x[4][4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint2 wv = *reinterpret_cast<const uint2 *>(conv_w + (long long)(ch0 + c) * 4);
+    w[c][0] = bf_lo(wv.x); w[c][1] = bf_hi(wv.x); w[c][2] = bf_lo(wv.y); w[c][3] = bf_hi(wv.y);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int s = t - 3 + j;
+    if (s < 0) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) x[j][c] = bf(conv_in[(long long)(ch0 + c) * 4 + 4 + s]);
+    } else {
+      const uint2 xv = *reinterpret_cast<const uint2 *>(qkv + (long long)s * ld + ch0);
+      x[j][0] = bf_lo(xv.x); x[j][1] = bf_hi(xv.x); x[j][2] = bf_lo(xv.y); x[j][3] = bf_hi(xv.y);
+    }
+  }
+  float y[4], ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float tot = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tot = fmaf(x[j][c], w[c][j], tot);
+    const float v = rbf(tot);
+    y[c] = rbf(v * (1.f / (1.f + expf(-v))));
+    ss = fmaf(y[c], y[c], ss);
+  }
+  float *dst;
+  if (p < 2 * HK) {
+    const float r = rsqrtf(warp_sum(ss) + 1e-6f) * (p < HK ? dk_scale : 1.f);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) y[c] *= r;
+    dst = (p < HK ? qn + ((long long)t * HK + p) * DK : kn + ((long long)t * HK + p - HK) * DK);
+  } else {
+    const int h = p - 2 * HK;
+    dst = vv + ((long long)t * HV + h) * DK;
+    if (lane == 0) {
+      const float bv = bf(bb[(long long)t * ld + h]), av = bf(aa[(long long)t * ld + h]);
+      beta[(long long)t * HV + h] = rbf(1.f / (1.f + expf(-bv)));
+      const float xa = av + bf(dt_bias[h]);
+      const float sp = xa > 20.f ? xa : log1pf(expf(xa));
+      glog[(long long)t * HV + h] = -expf(bf(a_log[h])) * sp;
+    }
+  }
+  *reinterpret_cast<float4 *>(dst + lane * 4) = make_float4(y[0], y[1], y[2], y[3]);
+}
+
+// The chunk-local matrices of one (chunk of 32 tokens, value head) (reference: _solve,
+// chunked.py:17-44): P (in-order prefix sums of g), the Gram matrices k_i.k_j and q_i.k_j,
+// T^-1 = (I + L)^-1 by forward substitution, M_ij = (A_i / A_j) q_i.k_j (j <= i), written as the
+// chunk's record. Thread (a, b) of the 16 x 16 grid computes entries (i, j) in {a, a + 16} x
+// {b, b + 16} of both Gram matrices, summing over d in order.
+__global__ void __launch_bounds__(256) delta_chunk_prep_kernel(const float *qn, const float *kn, const float *glog,
+                                                               const float *beta, float *rec, int HK, int HV, int T) {
+  constexpr int DK = 128, LD = DK + 4;
   const int chunk = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = chunk * kChunk, kh = h / (HV / HK);
-  __shared__ float ks[kChunk][129], qs[kChunk][129];
+  __shared__ __align__(16) float ks[kChunk][LD], qs[kChunk][LD];
   __shared__ float P[kChunk], bt[kChunk], Lm[kChunk][kChunk + 1], Qm[kChunk][kChunk + 1];
-  // 1a. conv + SiLU of the head's 384 channels (q, k of key head kh; v of value head h)
-  for (int lc = tid; lc < 3 * DK; lc += blockDim.x) {
-    const int part = lc / DK, d = lc % DK;
-    const int ch = (part == 0 ? kh : part == 1 ? HK + kh : 2 * HK + h) * DK + d;
-    float w[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) w[j] = bf(conv_w[(long long)ch * 4 + j]);
-    // eight tokens at a time: their eleven window inputs are loaded before the first use
-#pragma unroll 1
-    for (int t8 = 0; t8 < kChunk; t8 += 8) {
-      float x[11];
-#pragma unroll
-      for (int j = 0; j < 11; ++j) {
-        const int s = t0 + t8 - 3 + j;
-        x[j] = s < 0 ? bf(conv_in[(long long)ch * 4 + 4 + s]) : s < T ? bf(qkv[(long long)s * ld + ch]) : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int t = t8 + u, tok = t0 + t;
-        float tot = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) tot = fmaf(x[u + j], w[j], tot);
-        const float v = rbf(tot);
-        const float y = tok < T ? rbf(v * (1.f / (1.f + expf(-v)))) : 0.f;
-        if (part == 0) qs[t][d] = y;
-        else if (part == 1) ks[t][d] = y;
-        else if (tok < T) vv[((long long)tok * HV + h) * DK + d] = y;
-      }
-    }
+  for (int idx = tid; idx < kChunk * DK / 4; idx += blockDim.x) {
+    const int t = idx / (DK / 4), d4 = (idx % (DK / 4)) * 4, tok = t0 + t;
+    const long long src = ((long long)tok * HK + kh) * DK + d4;
+    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+    *reinterpret_cast<float4 *>(&ks[t][d4]) = tok < T ? *reinterpret_cast<const float4 *>(kn + src) : z;
+    *reinterpret_cast<float4 *>(&qs[t][d4]) = tok < T ? *reinterpret_cast<const float4 *>(qn + src) : z;
   }
-  // 1b. gates
   if (tid < kChunk) {
     const int tok = t0 + tid;
-    float g = 0.f, b = 0.f;
-    if (tok < T) {
-      const float bv = bf(bb[(long long)tok * ld + h]), av = bf(aa[(long long)tok * ld + h]);
-      b = rbf(1.f / (1.f + expf(-bv)));
-      const float x = av + bf(dt_bias[h]);
-      const float sp = x > 20.f ? x : log1pf(expf(x));
-      g = -expf(bf(a_log[h])) * sp;
-    }
-    P[tid] = g;
-    bt[tid] = b;
-  }
-  __syncthreads();
-  // 1c. l2 norms, warp w takes tokens w, w + 8, w + 16, w + 24
-  for (int t = warp; t < kChunk; t += 8) {
-    const int tok = t0 + t;
-    float sq = 0.f, sk = 0.f;
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const float a = qs[t][g * 32 + lane], b = ks[t][g * 32 + lane];
-      sq += warp_sum(a * a);
-      sk += warp_sum(b * b);
-    }
-    const float rq = rsqrtf(sq + 1e-6f), rk = rsqrtf(sk + 1e-6f);
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const int d = g * 32 + lane;
-      const float q = qs[t][d] * rq * dk_scale, k = ks[t][d] * rk;
-      qs[t][d] = q;
-      ks[t][d] = k;
-      if (tok < T) {
-        qn[((long long)tok * HV + h) * DK + d] = q;
-        kn[((long long)tok * HV + h) * DK + d] = k;
-      }
-    }
+    P[tid] = tok < T ? glog[(long long)tok * HV + h] : 0.f;
+    bt[tid] = tok < T ? beta[(long long)tok * HV + h] : 0.f;
   }
   __syncthreads();
   if (tid == 0) {
     float run = 0.f;
     for (int i = 0; i < kChunk; ++i) { run += P[i]; P[i] = run; }
   }
-  // 2. Gram rows i = 4 warp .. 4 warp + 3 against key j = lane, summed over d in order
-  float ag[4] = {0.f, 0.f, 0.f, 0.f}, aq[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int d = 0; d < DK; ++d) {
-    const float kj = ks[lane][d];
+  const int a = tid >> 4, b = tid & 15;
+  float g[2][2] = {{0.f, 0.f}, {0.f, 0.f}}, m[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+#pragma unroll 4
+  for (int d = 0; d < DK; d += 4) {
+    const float4 ki0 = *reinterpret_cast<const float4 *>(&ks[a][d]);
+    const float4 ki1 = *reinterpret_cast<const float4 *>(&ks[a + 16][d]);
+    const float4 qi0 = *reinterpret_cast<const float4 *>(&qs[a][d]);
+    const float4 qi1 = *reinterpret_cast<const float4 *>(&qs[a + 16][d]);
+    const float4 kj0 = *reinterpret_cast<const float4 *>(&ks[b][d]);
+    const float4 kj1 = *reinterpret_cast<const float4 *>(&ks[b + 16][d]);
+    const float4 ki[2] = {ki0, ki1}, qi[2] = {qi0, qi1}, kj[2] = {kj0, kj1};
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      ag[r] = fmaf(ks[warp * 4 + r][d], kj, ag[r]);
-      aq[r] = fmaf(qs[warp * 4 + r][d], kj, aq[r]);
-    }
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        g[r][c] = fmaf(ki[r].w, kj[c].w, fmaf(ki[r].z, kj[c].z, fmaf(ki[r].y, kj[c].y, fmaf(ki[r].x, kj[c].x, g[r][c]))));
+        m[r][c] = fmaf(qi[r].w, kj[c].w, fmaf(qi[r].z, kj[c].z, fmaf(qi[r].y, kj[c].y, fmaf(qi[r].x, kj[c].x, m[r][c]))));
+      }
   }
   __syncthreads();  // P complete
   float *out = rec + ((long long)chunk * HV + h) * kRecFloats;
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int i = warp * 4 + r, j = lane;
-    const float ratio = j <= i ? expf(P[i] - P[j]) : 0.f;
-    Lm[i][j] = j < i ? bt[i] * ratio * ag[r] : 0.f;
-    Qm[i][j] = j <= i ? ratio * aq[r] : 0.f;
-  }
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int i = a + 16 * r, j = b + 16 * c;
+      const float ratio = j <= i ? expf(P[i] - P[j]) : 0.f;
+      Lm[i][j] = j < i ? bt[i] * ratio * g[r][c] : 0.f;
+      Qm[i][j] = j <= i ? ratio * m[r][c] : 0.f;
+    }
   __syncthreads();
-  for (int idx = tid; idx < kChunk * kChunk; idx += blockDim.x) {
-    const int j = idx / kChunk, i = idx % kChunk;
-    out[REC_MO + idx] = Qm[i][j];
-  }
-  if (tid < kChunk) {
-    out[REC_A + tid] = expf(P[tid]);
-    out[REC_BETA + tid] = bt[tid];
-    out[REC_WS + tid] = expf(P[kChunk - 1] - P[tid]);
-    if (tid == 0) out[REC_ALAST] = expf(P[kChunk - 1]);
-  }
   if (warp == 0) {
     // row i of X = (I + L)^-1: X_i = e_i - sum_{j<i} L_ij X_j; lane c keeps column c of X
     float X[kChunk];
@@ -323,6 +327,18 @@ __global__ void __launch_bounds__(256) delta_chunk_prepare_kernel(
     }
 #pragma unroll
     for (int i = 0; i < kChunk; ++i) out[REC_TINV + lane * kChunk + i] = X[i];
+  } else {
+    for (int idx = tid - 32; idx < kChunk * kChunk; idx += blockDim.x - 32) {
+      const int j = idx / kChunk, i = idx % kChunk;
+      out[REC_MO + idx] = Qm[i][j];
+    }
+    if (tid >= 32 && tid < 32 + kChunk) {
+      const int i = tid - 32;
+      out[REC_A + i] = expf(P[i]);
+      out[REC_BETA + i] = bt[i];
+      out[REC_WS + i] = expf(P[kChunk - 1] - P[i]);
+      if (i == 0) out[REC_ALAST] = expf(P[kChunk - 1]);
+    }
   }
 }
 
@@ -382,19 +398,19 @@ __device__ __forceinline__ void project2(const float (*x)[128], int r0, const fl
 
 __global__ void __launch_bounds__(256, 2) delta_chunk_scan_kernel(const float *qn, const float *kn, const float *vv,
                                                                   const float *rec, const float *rec_in,
-                                                                  float *rec_out, bf16 *core, int HV, int T) {
+                                                                  float *rec_out, bf16 *core, int HK, int HV, int T) {
   constexpr int DK = 128;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   ChunkBuf *buf = reinterpret_cast<ChunkBuf *>(smem_raw);
   float(*obuf)[kScanCols] = reinterpret_cast<float(*)[kScanCols]>(smem_raw + 2 * sizeof(ChunkBuf));
   const int h = blockIdx.x, c0 = blockIdx.y * kScanCols, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int cw = 2 * warp, r0 = lane * 4;
+  const int cw = 2 * warp, r0 = lane * 4, kh = h / (HV / HK);
   const int nch = (T + kChunk - 1) / kChunk;
   auto issue = [&](int chunk, ChunkBuf &b) {
     const int t0 = chunk * kChunk;
     for (int idx = tid; idx < kChunk * DK / 4; idx += 256) {
       const int t = idx / (DK / 4), d4 = idx % (DK / 4), tok = t0 + t;
-      const long long src = ((long long)min(tok, T - 1) * HV + h) * DK + d4 * 4;
+      const long long src = ((long long)min(tok, T - 1) * HK + kh) * DK + d4 * 4;
       cp_async16(&b.k[t][d4 * 4], kn + src, tok < T);
       cp_async16(&b.q[t][d4 * 4], qn + src, tok < T);
     }
@@ -663,6 +679,7 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
     if (e_ != cudaSuccess) return xb::fail(XB_ERR_CUDA, std::string("prefill launch: ") + cudaGetErrorString(e_)); \
   } while (0)
   const int NP = proj_width(g);
+  if (NP % 4) return xb::fail(XB_ERR_UNSUPPORTED, "prefill needs projection rows of a multiple of 4 elements");
   bf16 *proj = P(L.proj);
   // One GEMM per group of projections that read the same rows when their weights are adjacent
   // rows of one tensor (the reference's packed layout), else one GEMM per projection, each into
@@ -699,14 +716,21 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
       const int HVD = HV * DK;
       XB_TRY(group(x, H, {{w.in_qkv, CH}, {w.in_z, HVD}, {w.in_b, HV}, {w.in_a, HV}}));
       const bf16 *qkv = proj, *z = proj + CH, *bb = proj + CH + HVD, *aa = proj + CH + HVD + HV;
-      delta_chunk_prepare_kernel<<<dim3((T + kChunk - 1) / kChunk, HV), 256, 0, st>>>(
-          qkv, bb, aa, NP, (const bf16 *)s.conv_in, (const bf16 *)w.conv_w, (const bf16 *)w.a_log,
-          (const bf16 *)w.dt_bias, F(L.qn), F(L.kn), F(L.vv), F(L.rec), HK, HV, T, (float)(1.0 / std::sqrt((double)DK)));
+      {
+        const long long warps = (long long)T * (2 * HK + HV);
+        delta_prepare_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
+            qkv, bb, aa, NP, (const bf16 *)s.conv_in, (const bf16 *)w.conv_w, (const bf16 *)w.a_log,
+            (const bf16 *)w.dt_bias, F(L.qn), F(L.kn), F(L.vv), F(L.beta), F(L.glog), HK, HV, T,
+            (float)(1.0 / std::sqrt((double)DK)));
+        XB_LAUNCHED();
+      }
+      delta_chunk_prep_kernel<<<dim3((T + kChunk - 1) / kChunk, HV), 256, 0, st>>>(F(L.qn), F(L.kn), F(L.glog),
+                                                                                F(L.beta), F(L.rec), HK, HV, T);
       XB_LAUNCHED();
       conv_state_kernel<<<(CH + 255) / 256, 256, 0, st>>>(qkv, NP, (const bf16 *)s.conv_in, (bf16 *)s.conv_out, CH, T);
       XB_LAUNCHED();
       delta_chunk_scan_kernel<<<dim3(HV, DK / kScanCols), 256, kScanSmem, st>>>(
-          F(L.qn), F(L.kn), F(L.vv), F(L.rec), (const float *)s.rec_in, (float *)s.rec_out, P(L.core), HV, T);
+          F(L.qn), F(L.kn), F(L.vv), F(L.rec), (const float *)s.rec_in, (float *)s.rec_out, P(L.core), HK, HV, T);
       XB_LAUNCHED();
       gated_norm_kernel<<<dim3(T, HV), 128, 0, st>>>(P(L.core), z, NP, (const bf16 *)w.gnorm, x2, HV, DK, g.rms_eps);
       XB_LAUNCHED();
