@@ -1575,6 +1575,7 @@ template <int NB> struct Consumer {
     const XbLayerWeights &w = p.layers[l];
     const unsigned tg = tag(l, 0);
     const int D = p.D, HQ = p.HQ, HKV = p.HKV, G = HQ / HKV, RD = p.RD;
+    const int P = kWarps / G;
     const bool q35 = p.family == XB_FAMILY_QWEN35;
     const int qrow = q35 ? 2 * D : D;
     const int koff = HQ * qrow, voff = koff + HKV * D;
@@ -1678,121 +1679,91 @@ template <int NB> struct Consumer {
         kc[(size_t)pos * D + tid] = tobf(kn[tid]);
         vc[(size_t)pos * D + tid] = tobf(vn[tid]);
       }
-      // split-KV partial over positions [j0, j1): warp w takes blocks of 32 positions
-      // w, w + 8, ... and every query head of the KV head. Scores with one position per lane
-      // (its K row read once for all G heads), one maximum and one rescale per block and head,
-      // then P.V with the lanes over the head dimension. FlashAttention-2 rounding: fp32 row
-      // sums of the fp32 probabilities, P rounded to bf16 for P.V.
-      constexpr int kMaxG = 4;
-      float o[kMaxG][8], m[kMaxG], lsum[kMaxG];
+      // split-KV partial over positions [j0, j1) for query head g = warp % G
+      const int g = warp % G, lane_pos = warp / G;
+      float q[8], o[8];
+      float m = -INFINITY, lsum = 0.f;
 #pragma unroll
-      for (int gg = 0; gg < kMaxG; ++gg) {
-        m[gg] = -INFINITY;
-        lsum[gg] = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[gg][e] = 0.f;
+      for (int e = 0; e < 8; ++e) {
+        o[e] = 0.f;
+        q[e] = e < EPL ? qs[g * D + lane * EPL + e] : 0.f;
       }
-      const int nblk = (j1 - j0 + 31) / 32;
-      for (int blk = warp; blk < nblk; blk += kWarps) {
-        const int jb = j0 + blk * 32, j = jb + lane;
-        const bool valid = j < j1;
-        float sc[kMaxG];
-#pragma unroll
-        for (int gg = 0; gg < kMaxG; ++gg) sc[gg] = 0.f;
-        if (valid) {
-          const bf16 *krow = kc + (size_t)j * D;
-          for (int c = 0; c < D; c += 8) {
-            float kf[8];
-            if (j == pos) {
-#pragma unroll
-              for (int e = 0; e < 8; ++e) kf[e] = kn[c + e];
-            } else {
-              unpack8(ldg_u4(krow + c), kf);
-            }
-#pragma unroll
-            for (int gg = 0; gg < kMaxG; ++gg)
-              if (gg < G) {
-                const float4 q0 = *reinterpret_cast<const float4 *>(qs + gg * D + c);
-                const float4 q1 = *reinterpret_cast<const float4 *>(qs + gg * D + c + 4);
-                float t = sc[gg];
-                t = fmaf(q0.x, kf[0], t); t = fmaf(q0.y, kf[1], t); t = fmaf(q0.z, kf[2], t); t = fmaf(q0.w, kf[3], t);
-                t = fmaf(q1.x, kf[4], t); t = fmaf(q1.y, kf[5], t); t = fmaf(q1.z, kf[6], t); t = fmaf(q1.w, kf[7], t);
-                sc[gg] = t;
-              }
-          }
-        }
-        float pb[kMaxG];
-#pragma unroll
-        for (int gg = 0; gg < kMaxG; ++gg)
-          if (gg < G) {
-            const float sv = valid ? sc[gg] * scale : -INFINITY;
-            const float mn = fmaxf(m[gg], warp_max(sv));
-            const float corr = expf(m[gg] - mn);
-            const float pe = valid ? expf(sv - mn) : 0.f;
-            lsum[gg] = fmaf(lsum[gg], corr, pe);
-            pb[gg] = rbf(pe);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) o[gg][e] *= corr;
-            m[gg] = mn;
-          }
-        const int cnt = min(32, j1 - jb);
-#pragma unroll 4
-        for (int jj = 0; jj < cnt; ++jj) {
-          const int jr = jb + jj;
-          float vf[8];
-          if (jr == pos) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) vf[e] = e < EPL ? vn[lane * EPL + e] : 0.f;
-          } else if (EPL == 8) {
-            unpack8(ldg_u4(vc + (size_t)jr * D + lane * 8), vf);
+      // one position per step, the next position's K/V rows prefetched (kept packed)
+      uint4 kraw = make_uint4(0, 0, 0, 0), vraw = kraw;
+      auto fetch = [&](int j, uint4 &kr4, uint4 &vr4) {
+        if (j < j1 && j != pos) {
+          if (EPL == 8) {
+            kr4 = ldg_u4(kc + (size_t)j * D + lane * 8);
+            vr4 = ldg_u4(vc + (size_t)j * D + lane * 8);
           } else {
-            const uint2 v2 = ldg_u2(vc + (size_t)jr * D + lane * 4);
-            unpack8(make_uint4(v2.x, v2.y, 0, 0), vf);
+            const uint2 k2 = ldg_u2(kc + (size_t)j * D + lane * 4);
+            const uint2 v2 = ldg_u2(vc + (size_t)j * D + lane * 4);
+            kr4 = make_uint4(k2.x, k2.y, 0, 0);
+            vr4 = make_uint4(v2.x, v2.y, 0, 0);
           }
-#pragma unroll
-          for (int gg = 0; gg < kMaxG; ++gg)
-            if (gg < G) {
-              const float pj = __shfl_sync(0xffffffffu, pb[gg], jj);
-#pragma unroll
-              for (int e = 0; e < 8; ++e)
-                if (e < EPL) o[gg][e] = fmaf(pj, vf[e], o[gg][e]);
-            }
         }
+      };
+      fetch(j0 + lane_pos, kraw, vraw);
+      for (int j = j0 + lane_pos; j < j1; j += P) {
+        const uint4 kcur = kraw, vcur = vraw;
+        fetch(j + P, kraw, vraw);
+        float kf[8], vf[8];
+        if (j == pos) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            kf[e] = e < EPL ? kn[lane * EPL + e] : 0.f;
+            vf[e] = e < EPL ? vn[lane * EPL + e] : 0.f;
+          }
+        } else {
+          unpack8(kcur, kf);
+          unpack8(vcur, vf);
+        }
+        float sc = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < EPL) sc = fmaf(q[e], kf[e], sc);
+        sc = warp_sum(sc) * scale;
+        const float mn = fmaxf(m, sc);
+        const float corr = expf(m - mn);
+        const float pe = expf(sc - mn);
+        lsum = lsum * corr + pe;
+        // FlashAttention-2 rounding: the row sum over fp32 probabilities, P.V over bf16 ones
+        const float pb = rbf(pe);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < EPL) o[e] = fmaf(pb, vf[e], o[e] * corr);
+        m = mn;
       }
       trace_mark(2);
-      // merge the warps' partial states, one query head at a time
+      // merge the P partial states of each head
       const int MS = D + 2;
       float *mw = mg + (size_t)warp * MS;
 #pragma unroll
-      for (int gg = 0; gg < kMaxG; ++gg) {
-        if (gg >= G) break;
-        const float lw = warp_sum(lsum[gg]);
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          if (e < EPL) mw[lane * EPL + e] = o[gg][e];
-        if (lane == 0) { mw[D] = m[gg]; mw[D + 1] = lw; }
-        csync();
-        for (int d = tid; d < D; d += kCT) {
-          float M = -INFINITY;
-          for (int i = 0; i < kWarps; ++i) M = fmaxf(M, mg[(size_t)i * MS + D]);
-          float O = 0.f, Lw = 0.f;
-          if (M != -INFINITY) {
-            for (int i = 0; i < kWarps; ++i) {
-              const float *ms = mg + (size_t)i * MS;
-              const float mi = ms[D];
-              if (mi == -INFINITY) continue;
-              const float f = expf(mi - M);
-              O = fmaf(ms[d], f, O);
-              Lw = fmaf(ms[D + 1], f, Lw);
-            }
+      for (int e = 0; e < 8; ++e)
+        if (e < EPL) mw[lane * EPL + e] = o[e];
+      if (lane == 0) { mw[D] = m; mw[D + 1] = lsum; }
+      csync();
+      for (int idx = tid; idx < G * D; idx += kCT) {
+        const int gg = idx / D, d = idx % D;
+        float M = -INFINITY;
+        for (int i = 0; i < P; ++i) M = fmaxf(M, mg[(size_t)(i * G + gg) * MS + D]);
+        float O = 0.f, Lw = 0.f;
+        if (M != -INFINITY) {
+          for (int i = 0; i < P; ++i) {
+            const float *ms = mg + (size_t)(i * G + gg) * MS;
+            const float mi = ms[D];
+            if (mi == -INFINITY) continue;
+            const float f = expf(mi - M);
+            O = fmaf(ms[d], f, O);
+            Lw = fmaf(ms[D + 1], f, Lw);
           }
-          const int hq = kvh * G + gg;
-          const size_t base = ((size_t)b * HQ + hq) * splits + s;
-          st_u64(p.att_o + base * D + d, ftag(O, tg));
-          if (d == 0) st_u64x2(p.att_ml + 2 * base, ftag(M, tg), ftag(Lw, tg));
         }
-        csync();
+        const int hq = kvh * G + gg;
+        const size_t base = ((size_t)b * HQ + hq) * splits + s;
+        st_u64(p.att_o + base * D + d, ftag(O, tg));
+        if (d == 0) st_u64x2(p.att_ml + 2 * base, ftag(M, tg), ftag(Lw, tg));
       }
+      csync();
     }
   }
 
