@@ -6,8 +6,8 @@
 // The kernel is CUTLASS's SM100 warp-specialised GEMM (cute/CUTLASS 4.x templates): TMA tile
 // loads of A and B into shared memory, MMAs issued by one thread with tcgen05.mma into a TMEM
 // accumulator, a TMA-store epilogue. With a 2-SM tile (cta_group::2, cluster 2x1x1) each CTA of
-// the pair loads its own half of the operands (cp.async.bulk.tensor.cta_group::2, no multicast);
-// 1-SM tiles run with cluster 1x1x1. Each translation unit instantiates one configuration.
+// the pair loads only its own half of the operands, with the cta_group::2 form of the tiled
+// load; 1-SM tiles run with cluster 1x1x1. Each translation unit instantiates one configuration.
 #pragma once
 
 #include "cutlass/cutlass.h"

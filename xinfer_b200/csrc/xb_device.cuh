@@ -216,7 +216,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
 }
 
 // One-dimensional bulk copy global -> this CTA's shared memory, completing on `bar`.
-// Both addresses 16-byte aligned, `bytes` a multiple of 16. No multicast.
+// Both addresses 16-byte aligned, `bytes` a multiple of 16; the destination is this CTA only.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar,
                                          uint64_t policy) {
   asm volatile(
