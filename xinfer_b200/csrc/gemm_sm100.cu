@@ -62,7 +62,19 @@ int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, 
   // measured on B200 over the prefill shapes of Qwen3.5-0.8B / 4B at 512 tokens
   if (m <= 64) return run_rows(m, n, k, x, w, out, ldo, st, device);
   if (n < 2048) return run_narrow(m, n, k, x, w, out, ldo, st, device);
-  return run_wide(m, n, k, x, w, out, ldo, st, device);
+  // the width whose tiles need the fewest waves over the SMs, time ~ waves x width (wider on ties)
+  static int sms = 0;
+  if (!sms && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) sms = 148;
+  const int widths[3] = {256, 192, 128};
+  const RunFn fns[3] = {run_wide256, run_wide192, run_wide128};
+  int best = 0;
+  long long best_cost = -1;
+  for (int i = 0; i < 3; ++i) {
+    const long long tiles = (long long)((m + 127) / 128) * ((n + widths[i] - 1) / widths[i]);
+    const long long cost = (tiles + sms - 1) / sms * widths[i];
+    if (best_cost < 0 || cost < best_cost) { best = i; best_cost = cost; }
+  }
+  return fns[best](m, n, k, x, w, out, ldo, st, device);
 }
 
 extern "C" int xb_gemm_bf16(int32_t m, int32_t n, int32_t k, const void *x, const void *w, void *out,

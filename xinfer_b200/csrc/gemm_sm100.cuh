@@ -5,9 +5,8 @@
 //
 // The kernel is CUTLASS's SM100 warp-specialised GEMM (cute/CUTLASS 4.x templates): TMA tile
 // loads of A and B into shared memory, MMAs issued by one thread with tcgen05.mma into a TMEM
-// accumulator, a TMA-store epilogue. With a 2-SM tile (cta_group::2, cluster 2x1x1) each CTA of
-// the pair loads only its own half of the operands, with the cta_group::2 form of the tiled
-// load; 1-SM tiles run with cluster 1x1x1. Each translation unit instantiates one configuration.
+// accumulator, a TMA-store epilogue. Every configuration runs one CTA per cluster (1 x 1 x 1), so
+// each CTA loads its own operand tiles. Each translation unit instantiates one configuration.
 #pragma once
 
 #include "cutlass/cutlass.h"
@@ -36,30 +35,29 @@ using LayoutD = cutlass::layout::RowMajor;     // out [M, N]
 using Accumulator = float;
 constexpr int kAlign = 8;  // 16-byte rows
 
-template <class TileShape, class ClusterShape, class MainloopSchedule, class EpilogueSchedule> struct Config {
+template <class TileShape> struct Config {
   using Epilogue = typename cutlass::epilogue::collective::CollectiveBuilder<
-      cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, TileShape, ClusterShape,
+      cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, TileShape, cute::Shape<cute::_1, cute::_1, cute::_1>,
       cutlass::epilogue::collective::EpilogueTileAuto, Accumulator, Accumulator, void, LayoutD, kAlign, ElementD,
-      LayoutD, kAlign, EpilogueSchedule>::CollectiveOp;
+      LayoutD, kAlign, cutlass::epilogue::TmaWarpSpecialized1Sm>::CollectiveOp;
   using Mainloop = typename cutlass::gemm::collective::CollectiveBuilder<
       cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, ElementA, LayoutA, kAlign, ElementB, LayoutB, kAlign,
-      Accumulator, TileShape, ClusterShape,
+      Accumulator, TileShape, cute::Shape<cute::_1, cute::_1, cute::_1>,
       cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(sizeof(typename Epilogue::SharedStorage))>,
-      MainloopSchedule>::CollectiveOp;
+      cutlass::gemm::KernelTmaWarpSpecialized1SmSm100>::CollectiveOp;
   using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue>;
   using Gemm = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
 };
 
-// 2-SM pairs of 256 x 128 output tiles: the wide projections (the best of the measured tiles for
-// every prefill shape with N >= 2048)
-using Wide = Config<Shape<_256, _128, _64>, Shape<_2, _1, _1>, cutlass::gemm::KernelTmaWarpSpecialized2SmSm100,
-                    cutlass::epilogue::TmaWarpSpecialized2Sm>;
-// 64 x 64 tiles: narrow outputs (N < 2048) over long K, where wider tiles leave most SMs idle
-using Narrow = Config<Shape<_64, _64, _64>, Shape<_1, _1, _1>, cutlass::gemm::KernelTmaWarpSpecialized1SmSm100,
-                      cutlass::epilogue::TmaWarpSpecialized1Sm>;
-// 64 x 128 tiles: a few rows (the last token's lm_head)
-using Rows = Config<Shape<_64, _128, _64>, Shape<_1, _1, _1>, cutlass::gemm::KernelTmaWarpSpecialized1SmSm100,
-                    cutlass::epilogue::TmaWarpSpecialized1Sm>;
+// Tiles (tokens x weight rows x K), chosen from a sweep on B200 over the Qwen3.5-0.8B / 4B
+// prefill shapes at 512 tokens: 128-row tiles of 128, 192 or 256 weight rows for the wide
+// projections (the width that needs the fewest tile waves), 64 x 64 for narrow outputs over long
+// K (N < 2048), 64 x 128 for a few rows (the last token's lm_head).
+using Wide128 = Config<Shape<_128, _128, _64>>;
+using Wide192 = Config<Shape<_128, _192, _64>>;
+using Wide256 = Config<Shape<_128, _256, _64>>;
+using Narrow = Config<Shape<_64, _64, _64>>;
+using Rows = Config<Shape<_64, _128, _64>>;
 
 // Launch parameters (TMA descriptors included) of every (shape, operands, device) seen: a prefill
 // chunk runs the same GEMMs on the same buffers again and again, and building the descriptors is
@@ -122,9 +120,12 @@ int run(int m, int n, int k, const void *x, const void *w, void *out, long long 
   return XB_OK;
 }
 
-// one instantiation per translation unit (gemm_sm100.cu, gemm_sm100_wide.cu)
-int run_wide(int m, int n, int k, const void *x, const void *w, void *out, long long ldo, cudaStream_t st, int device);
-int run_narrow(int m, int n, int k, const void *x, const void *w, void *out, long long ldo, cudaStream_t st,
-               int device);
-int run_rows(int m, int n, int k, const void *x, const void *w, void *out, long long ldo, cudaStream_t st, int device);
+// one instantiation per translation unit (gemm_sm100.cu, gemm_sm100_w*.cu)
+using RunFn = int (*)(int m, int n, int k, const void *x, const void *w, void *out, long long ldo, cudaStream_t st,
+                      int device);
+int run_wide128(int, int, int, const void *, const void *, void *, long long, cudaStream_t, int);
+int run_wide192(int, int, int, const void *, const void *, void *, long long, cudaStream_t, int);
+int run_wide256(int, int, int, const void *, const void *, void *, long long, cudaStream_t, int);
+int run_narrow(int, int, int, const void *, const void *, void *, long long, cudaStream_t, int);
+int run_rows(int, int, int, const void *, const void *, void *, long long, cudaStream_t, int);
 } // namespace xbgemm

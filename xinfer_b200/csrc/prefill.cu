@@ -94,12 +94,12 @@ __global__ void embed_kernel(const int64_t *ids, const bf16 *embed, bf16 *h, int
 
 // Residual add and RMSNorm of rows: with `o`, h = bf16(h + o) first (the reference's residual
 // add, both operands bf16) and h is written back; then out = RMSNorm(h) (HF Qwen3RMSNorm:
-// w * bf16(x r); Qwen3_5RMSNorm: bf16(x r (1 + w))). 256 threads per row, each summing the
+// w * bf16(x r); Qwen3_5RMSNorm: bf16(x r (1 + w))). 128 or 256 threads per row, each summing the
 // squares of its 8-element chunks c and c + 256 in order. Row blockIdx.x + row0 of h is
 // normalised into row blockIdx.x of out.
 __global__ void __launch_bounds__(256) add_rmsnorm_kernel(bf16 *h, const bf16 *o, const bf16 *w, bf16 *out, int H,
                                                           float eps, int q35, int row0) {
-  const int t = blockIdx.x + row0, tid = threadIdx.x, nc = H / 8;
+  const int t = blockIdx.x + row0, tid = threadIdx.x, nc = H / 8, nt = blockDim.x;
   uint4 *row = reinterpret_cast<uint4 *>(h + (long long)t * H);
   const uint4 *orow = o ? reinterpret_cast<const uint4 *>(o + (long long)t * H) : nullptr;
   __shared__ float red[8];
@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(bf16 *h, const bf16 *o
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    const int c = tid + i * 256;
+    const int c = tid + i * nt;
     xv[i] = c < nc ? row[c] : make_uint4(0, 0, 0, 0);
     float x[8];
     unpack8(xv[i], x);
@@ -126,13 +126,12 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(bf16 *h, const bf16 *o
   if ((tid & 31) == 0) red[tid >> 5] = ss;
   __syncthreads();
   float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) tot += red[i];
+  for (int i = 0; i < (nt >> 5); ++i) tot += red[i];
   const float r = rsqrtf(tot / (float)H + eps);
   uint4 *dst = reinterpret_cast<uint4 *>(out + (long long)blockIdx.x * H);
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    const int c = tid + i * 256;
+    const int c = tid + i * nt;
     if (c >= nc) continue;
     float x[8], wf[8], y[8];
     unpack8(xv[i], x);
@@ -145,22 +144,21 @@ __global__ void __launch_bounds__(256) add_rmsnorm_kernel(bf16 *h, const bf16 *o
 
 // act = bf16(bf16(silu(gate)) * up) (HF SiLU on a bf16 tensor, then the bf16 product), 8 values
 // per thread; gate and up are the two halves of each [gate | up] projection row.
-__global__ void silu_mul_kernel(const bf16 *proj, bf16 *act, int I, int ld, int T) {
+__global__ void __launch_bounds__(256) silu_mul_kernel(const bf16 *proj, bf16 *act, int I, int ld, int T) {
   const int n8 = I / 8;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)T * n8;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long t = i / n8;
-    const int c = (int)(i % n8);
-    const uint4 gv = reinterpret_cast<const uint4 *>(proj + t * ld)[c];
-    const uint4 uv = reinterpret_cast<const uint4 *>(proj + t * ld + I)[c];
-    float g[8], u[8], y[8];
-    unpack8(gv, g);
-    unpack8(uv, u);
+  const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (i >= (long long)T * n8) return;
+  const long long t = i / n8;
+  const int c = (int)(i % n8);
+  const uint4 gv = reinterpret_cast<const uint4 *>(proj + t * ld)[c];
+  const uint4 uv = reinterpret_cast<const uint4 *>(proj + t * ld + I)[c];
+  float g[8], u[8], y[8];
+  unpack8(gv, g);
+  unpack8(uv, u);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) y[e] = rbf(g[e] / (1.f + expf(-g[e]))) * u[e];
-    reinterpret_cast<uint4 *>(act + t * I)[c] =
-        make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]), pack2(y[6], y[7]));
-  }
+  for (int e = 0; e < 8; ++e) y[e] = rbf(g[e] / (1.f + expf(-g[e]))) * u[e];
+  reinterpret_cast<uint4 *>(act + t * I)[c] =
+      make_uint4(pack2(y[0], y[1]), pack2(y[2], y[3]), pack2(y[4], y[5]), pack2(y[6], y[7]));
 }
 
 // The conv window after the last token: the last four inputs of [old window, tokens] for every
@@ -495,25 +493,40 @@ __global__ void __launch_bounds__(256, 2) delta_chunk_scan_kernel(const float *q
     for (int r = 0; r < 4; ++r) So[(long long)(r0 + r) * DK + c0 + cw + c] = S[c][r];
 }
 
-// Gated RMSNorm of token t, head h (HF Qwen3_5RMSNormGated): bf16(bf16(w * bf16(x r)) * silu(z)),
-// the sum of squares taken like the decode kernel's: per 16-value tile, then
-// ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)).
-__global__ void __launch_bounds__(128) gated_norm_kernel(const bf16 *core, const bf16 *z, int ld, const bf16 *w,
-                                                         bf16 *out, int HV, int DK, float eps) {
-  const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
-  const long long i = ((long long)t * HV + h) * DK + tid;
-  __shared__ float part[8];
-  const float x = bf(core[i]);
-  float sq = x * x;
+// Gated RMSNorm (HF Qwen3_5RMSNormGated): bf16(bf16(w * bf16(x r)) * silu(z)) over each head's
+// 128 values, one warp per (token, head), lane l holding values 4l..4l + 3; the sum of squares is
+// taken like the decode kernel's: per 16-value tile, then ((p0 + p1) + (p2 + p3)) + ((p4 + p5) +
+// (p6 + p7)).
+__global__ void __launch_bounds__(256) gated_norm_kernel(const bf16 *core, const bf16 *z, int ld, const bf16 *w,
+                                                         bf16 *out, int HV, int T, float eps) {
+  constexpr int DK = 128;
+  const int lane = threadIdx.x & 31;
+  const long long unit = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (unit >= (long long)T * HV) return;
+  const long long t = unit / HV;
+  const int h = (int)(unit % HV);
+  const long long i = unit * DK + lane * 4;
+  const uint2 xv = *reinterpret_cast<const uint2 *>(core + i);
+  const uint2 zv = *reinterpret_cast<const uint2 *>(z + t * ld + h * DK + lane * 4);
+  const uint2 wv = *reinterpret_cast<const uint2 *>(w + lane * 4);
+  const float x[4] = {bf_lo(xv.x), bf_hi(xv.x), bf_lo(xv.y), bf_hi(xv.y)};
+  const float zz[4] = {bf_lo(zv.x), bf_hi(zv.x), bf_lo(zv.y), bf_hi(zv.y)};
+  const float wf[4] = {bf_lo(wv.x), bf_hi(wv.x), bf_lo(wv.y), bf_hi(wv.y)};
+  float sq = fmaf(x[3], x[3], fmaf(x[2], x[2], fmaf(x[1], x[1], x[0] * x[0])));
+  sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+  sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+  float p[8];
 #pragma unroll
-  for (int o = 8; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-  if ((tid & 15) == 0) part[tid >> 4] = sq;
-  __syncthreads();
-  const float tot = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+  for (int k = 0; k < 8; ++k) p[k] = __shfl_sync(0xffffffffu, sq, 4 * k);
+  const float tot = ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
   const float r = rsqrtf(tot / (float)DK + eps);
-  const float n = rbf(bf(w[tid]) * rbf(x * r));
-  const float zz = bf(z[(long long)t * ld + h * DK + tid]);
-  out[i] = tobf(n * (zz / (1.f + expf(-zz))));
+  float y[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float n = rbf(wf[e] * rbf(x[e] * r));
+    y[e] = n * (zz[e] / (1.f + expf(-zz[e])));
+  }
+  *reinterpret_cast<uint2 *>(out + i) = make_uint2(pack2(y[0], y[1]), pack2(y[2], y[3]));
 }
 
 // q/k RMSNorm over the head dim and RoPE (rotate-half over the first RD dims, bf16 cos/sin of
@@ -703,10 +716,10 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
     }
     return XB_OK;
   };
-  const int eb = 296;  // elementwise grid: 2 CTAs per SM
+  const int rn = H / 8 <= 128 ? 128 : 256;  // threads per row of the add + RMSNorm kernel
   embed_kernel<<<T, 128, 0, st>>>(a->input_ids, (const bf16 *)model->w.embed, h, H, g.vocab, err);
   XB_LAUNCHED();
-  add_rmsnorm_kernel<<<T, 256, 0, st>>>(h, nullptr, (const bf16 *)model->w.layers[0].input_norm, x, H, g.rms_eps,
+  add_rmsnorm_kernel<<<T, rn, 0, st>>>(h, nullptr, (const bf16 *)model->w.layers[0].input_norm, x, H, g.rms_eps,
                                         q35, 0);
   XB_LAUNCHED();
   for (int l = 0; l < g.num_layers; ++l) {
@@ -732,7 +745,9 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
       delta_chunk_scan_kernel<<<dim3(HV, DK / kScanCols), 256, kScanSmem, st>>>(
           F(L.qn), F(L.kn), F(L.vv), F(L.rec), (const float *)s.rec_in, (float *)s.rec_out, P(L.core), HK, HV, T);
       XB_LAUNCHED();
-      gated_norm_kernel<<<dim3(T, HV), 128, 0, st>>>(P(L.core), z, NP, (const bf16 *)w.gnorm, x2, HV, DK, g.rms_eps);
+      gated_norm_kernel<<<(unsigned)(((long long)T * HV + 7) / 8), 256, 0, st>>>(P(L.core), z, NP,
+                                                                              (const bf16 *)w.gnorm, x2, HV, T,
+                                                                              g.rms_eps);
       XB_LAUNCHED();
       XB_TRY(xb::gemm_bf16(T, H, HVD, x2, w.out_proj, out, H, stream));
     } else {
@@ -763,18 +778,18 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
       XB_LAUNCHED();
       XB_TRY(xb::gemm_bf16(T, H, HQ * D, x2, w.o_proj, out, H, stream));
     }
-    add_rmsnorm_kernel<<<T, 256, 0, st>>>(h, out, (const bf16 *)w.post_norm, x, H, g.rms_eps, q35, 0);
+    add_rmsnorm_kernel<<<T, rn, 0, st>>>(h, out, (const bf16 *)w.post_norm, x, H, g.rms_eps, q35, 0);
     XB_LAUNCHED();
     XB_TRY(group(x, H, {{w.gate, I}, {w.up, I}}));
-    silu_mul_kernel<<<eb, 256, 0, st>>>(proj, x2, I, NP, T);
+    silu_mul_kernel<<<(unsigned)(((long long)T * (I / 8) + 255) / 256), 256, 0, st>>>(proj, x2, I, NP, T);
     XB_LAUNCHED();
     XB_TRY(xb::gemm_bf16(T, H, I, x2, w.down, out, H, stream));
     if (l + 1 < g.num_layers) {
-      add_rmsnorm_kernel<<<T, 256, 0, st>>>(h, out, (const bf16 *)model->w.layers[l + 1].input_norm, x, H,
+      add_rmsnorm_kernel<<<T, rn, 0, st>>>(h, out, (const bf16 *)model->w.layers[l + 1].input_norm, x, H,
                                             g.rms_eps, q35, 0);
     } else {
       // the last token only: residual add, final norm (ModelStep's last-token gather, model.py:178-183)
-      add_rmsnorm_kernel<<<1, 256, 0, st>>>(h, out, (const bf16 *)model->w.final_norm, P(L.xlast), H, g.rms_eps,
+      add_rmsnorm_kernel<<<1, rn, 0, st>>>(h, out, (const bf16 *)model->w.final_norm, P(L.xlast), H, g.rms_eps,
                                             q35, T - 1);
     }
     XB_LAUNCHED();
