@@ -29,15 +29,6 @@ BUILD_DIR = PKG / "_build"  # object files (not committed)
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
-def cutlass_includes():
-    """CUTLASS / CuTe header trees (4.x, with the SM100 collectives) vendored in this image."""
-    import flashinfer  # the header tree ships as package data
-
-    root = Path(flashinfer.__file__).resolve().parent / "data" / "cutlass"
-    inc = [root / "include", root / "tools" / "util" / "include"]
-    if not all((p / "cutlass").is_dir() for p in inc):
-        raise RuntimeError(f"CUTLASS headers not found under {root}")
-    return [f"-I{p}" for p in inc]
 FLAGS_CU = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr", "-Xptxas", "-v"]
 
 
@@ -83,7 +74,7 @@ def build_ops(force=False):
 
 
 def headers():
-    return sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+    return sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(INCLUDE.glob("*.h"))
 
 
 def up_to_date():
@@ -99,7 +90,7 @@ def _compile(src, obj, force):
     newest = max([src.stat().st_mtime] + [h.stat().st_mtime for h in headers()])
     if not force and obj.exists() and obj.stat().st_mtime >= newest:
         return ""
-    cmd = [nvcc(), *ARCH, *FLAGS_CU, f"-I{INCLUDE}", f"-I{CSRC}", *cutlass_includes(), "-c", "-o", str(obj) + ".tmp",
+    cmd = [nvcc(), *ARCH, *FLAGS_CU, f"-I{INCLUDE}", f"-I{CSRC}", "-c", "-o", str(obj) + ".tmp",
            str(src)]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     log = proc.stdout + proc.stderr

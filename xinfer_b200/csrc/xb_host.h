@@ -22,6 +22,8 @@ namespace xb {
 // Records `msg` as the calling thread's last error and returns `code`.
 int fail(int code, const std::string &msg);
 // out[m, n] (rows ldo elements apart) = x[m, k] . w[n, k]^T in bf16 with fp32 accumulation
-// (gemm_sm100.cu); xb_gemm_bf16 is the packed case ldo = n.
-int gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, long long ldo, void *stream);
+// (gemm_tc.cu); xb_gemm_bf16 is the packed case ldo = n. A device-side wait that expired sets
+// bit 0 of *err (a library-wide word when err is null).
+int gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, long long ldo, void *stream,
+              unsigned *err);
 } // namespace xb
