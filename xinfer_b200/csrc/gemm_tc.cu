@@ -16,6 +16,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -135,10 +136,13 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<const uint32_t *>(&v);
 }
 
+// Split-K (gridDim.z = S > 1): CTA z accumulates k-blocks [z nk / S, (z + 1) nk / S) and writes
+// its fp32 tile to part[z]; the CTA that arrives last at the tile's ticket (no waiting) adds the S
+// partial tiles in order z = 0..S-1, rounds once and stores, then resets the ticket.
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w, int M, int N,
-                int K, __nv_bfloat16 *out, long long ldo, unsigned *err) {
+                int K, __nv_bfloat16 *out, long long ldo, unsigned *err, float *part, unsigned *tickets) {
   using S = Shape<BN>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *base = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -148,7 +152,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned *tmem_slot = reinterpret_cast<unsigned *>(accum + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
-  const int nk = (K + kBK - 1) / kBK;
+  const int nk_all = (K + kBK - 1) / kBK, nsplit = gridDim.z;
+  const int kb0 = (int)((long long)nk_all * blockIdx.z / nsplit);
+  const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / nsplit) - kb0;
   if (!err) err = &g_error;
 
   if (threadIdx.x == 0) {
@@ -178,8 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         unsigned char *a = base + s * S::kStageBytes;
         unsigned char *b = a + kBM * kBK * 2;
         mbar_expect_tx(&full[s], S::kStageBytes);
-        tma_load_2d(a, &map_x, kb * kBK, m0, &full[s]);
-        tma_load_2d(b, &map_w, kb * kBK, n0, &full[s]);
+        tma_load_2d(a, &map_x, (kb0 + kb) * kBK, m0, &full[s]);
+        tma_load_2d(b, &map_w, (kb0 + kb) * kBK, n0, &full[s]);
       }
     }
   } else if (warp == 1) {
@@ -204,22 +210,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_wait(accum, 0, err);
     tmem_fence_after();
     const int row = m0 + quarter * 32 + lane;
+    auto store = [&](int c, const float *v) {
+      if (row >= M) return;
+      __nv_bfloat16 *dst = out + (long long)row * ldo + n0 + c;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (n0 + c + 8 * q < N) {
+          uint4 u;
+          u.x = pack_bf16(v[8 * q + 0], v[8 * q + 1]);
+          u.y = pack_bf16(v[8 * q + 2], v[8 * q + 3]);
+          u.z = pack_bf16(v[8 * q + 4], v[8 * q + 5]);
+          u.w = pack_bf16(v[8 * q + 6], v[8 * q + 7]);
+          *reinterpret_cast<uint4 *>(dst + 8 * q) = u;
+        }
+    };
+    // partial tile z: [row within tile][column], BN fp32 per row
+    const long long tile = (long long)blockIdx.y * gridDim.x + blockIdx.x;
+    auto slot = [&](int z) {
+      return part + (((long long)z * gridDim.x * gridDim.y + tile) * kBM + quarter * 32 + lane) * BN;
+    };
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
       uint32_t r[32];
       tmem_ld32(tmem + ((unsigned)(quarter * 32) << 16) + c, r);
-      if (row < M) {
-        __nv_bfloat16 *dst = out + (long long)row * ldo + n0 + c;
+      float v[32];
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          if (n0 + c + 8 * q < N) {
-            uint4 v;
-            v.x = pack_bf16(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
-            v.y = pack_bf16(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
-            v.z = pack_bf16(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
-            v.w = pack_bf16(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
-            *reinterpret_cast<uint4 *>(dst + 8 * q) = v;
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      if (nsplit == 1) {
+        store(c, v);
+      } else {
+        float4 *dst = reinterpret_cast<float4 *>(slot(blockIdx.z) + c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+    }
+    if (nsplit > 1) {
+      __shared__ unsigned last;
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) last = atomicAdd(&tickets[tile], 1u) == (unsigned)nsplit - 1;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (last) {
+        __threadfence();
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+          for (int z = 0; z < nsplit; ++z) {
+            const float4 *src = reinterpret_cast<const float4 *>(slot(z) + c);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 f = __ldcg(src + i);
+              v[4 * i] += f.x; v[4 * i + 1] += f.y; v[4 * i + 2] += f.z; v[4 * i + 3] += f.w;
+            }
           }
+          store(c, v);
+        }
+        if (threadIdx.x == 64) tickets[tile] = 0;
       }
     }
   }
@@ -315,24 +363,27 @@ constexpr size_t kMaxPlans = 4096;
 std::mutex plan_mu;
 std::unordered_map<PlanKey, Plan, PlanHash> plans;
 
-template <int BN> int launch(const Plan &p, int m, int n, int k, void *out, long long ldo, unsigned *err, cudaStream_t st) {
+template <int BN>
+int launch(const Plan &p, int m, int n, int k, void *out, long long ldo, unsigned *err, int splits, float *part,
+           unsigned *tickets, cudaStream_t st) {
   static std::once_flag attr;
   static cudaError_t attr_rc = cudaSuccess;
   std::call_once(attr, [] {
     attr_rc = cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape<BN>::kSmem);
   });
   if (attr_rc != cudaSuccess) return xb::fail(XB_ERR_CUDA, std::string("GEMM: ") + cudaGetErrorString(attr_rc));
-  const dim3 grid((n + BN - 1) / BN, (m + kBM - 1) / kBM);
+  const dim3 grid((n + BN - 1) / BN, (m + kBM - 1) / kBM, splits);
   gemm_kernel<BN><<<grid, kThreads, Shape<BN>::kSmem, st>>>(p.mx, p.mw, m, n, k, static_cast<__nv_bfloat16 *>(out),
-                                                             ldo, err);
+                                                             ldo, err, part, tickets);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? XB_OK : xb::fail(XB_ERR_CUDA, std::string("GEMM launch: ") + cudaGetErrorString(e));
 }
 
 // The tile width whose tiles need the fewest waves over the SMs (time ~ waves x width; the wider
-// on ties); N < 2048 (narrow outputs over long K) takes 64-wide tiles for more CTAs.
-int choose_bn(int m, int n, int sms) {
-  if (n < 2048) return 64;
+// on ties); narrow outputs (512 <= N < 2048, long K) take 128-wide tiles split over K when a
+// split-K workspace is given, else (and below 512) 64-wide tiles for more CTAs.
+int choose_bn(int m, int n, int sms, bool split) {
+  if (n < 2048) return split && n >= 512 ? 128 : 64;
   const int widths[3] = {256, 128, 64};
   int best = 256;
   long long best_cost = -1;
@@ -347,7 +398,7 @@ int choose_bn(int m, int n, int sms) {
 } // namespace xbtc
 
 int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, long long ldo, void *stream,
-                  unsigned *err) {
+                  unsigned *err, void *split_ws, size_t split_ws_bytes) {
   using namespace xbtc;
   if (m < 1 || n < 1 || k < 1 || !x || !w || !out || ldo < n) return xb::fail(XB_ERR_INVALID, "invalid GEMM arguments");
   if (k % 8) return xb::fail(XB_ERR_INVALID, "GEMM K must be a multiple of 8");
@@ -376,21 +427,38 @@ int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, 
   if (!found) {
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    plan.bn = choose_bn(m, n, sms);
+    plan.bn = choose_bn(m, n, sms, split_ws != nullptr);
     if (!make_map(&plan.mx, x, m, k, kBM) || !make_map(&plan.mw, w, n, k, plan.bn))
       return xb::fail(XB_ERR_CUDA, "GEMM: tensor map creation failed");
     std::lock_guard<std::mutex> lock(plan_mu);
     if (plans.size() >= kMaxPlans) plans.clear();
     plans.emplace(key, plan);
   }
+  // narrow outputs: split K so that about one CTA per SM streams K / S of the operands
+  int splits = 1;
+  float *part = nullptr;
+  unsigned *tickets = nullptr;
+  const long long tiles = (long long)((n + plan.bn - 1) / plan.bn) * ((m + kBM - 1) / kBM);
+  if (split_ws && n < 2048 && n >= 512) {
+    const int nk = (k + kBK - 1) / kBK;
+    splits = (int)std::min<long long>(std::min(8, nk / 4), std::max<long long>(1, 148 / tiles));
+    const size_t need = (size_t)splits * tiles * kBM * plan.bn * 4 + (size_t)tiles * 4;
+    if (splits < 2 || need > split_ws_bytes) {
+      splits = 1;
+    } else {
+      part = static_cast<float *>(split_ws);
+      const size_t part_bytes = (size_t)splits * tiles * kBM * plan.bn * 4;
+      tickets = reinterpret_cast<unsigned *>(static_cast<char *>(split_ws) + part_bytes);
+    }
+  }
   switch (plan.bn) {
-    case 256: return launch<256>(plan, m, n, k, out, ldo, err, st);
-    case 128: return launch<128>(plan, m, n, k, out, ldo, err, st);
-    default: return launch<64>(plan, m, n, k, out, ldo, err, st);
+    case 256: return launch<256>(plan, m, n, k, out, ldo, err, splits, part, tickets, st);
+    case 128: return launch<128>(plan, m, n, k, out, ldo, err, splits, part, tickets, st);
+    default: return launch<64>(plan, m, n, k, out, ldo, err, splits, part, tickets, st);
   }
 }
 
 extern "C" int xb_gemm_bf16(int32_t m, int32_t n, int32_t k, const void *x, const void *w, void *out,
                             void *stream) {
-  return xb::gemm_bf16(m, n, k, x, w, out, n, stream, nullptr);
+  return xb::gemm_bf16(m, n, k, x, w, out, n, stream, nullptr, nullptr, 0);
 }
