@@ -442,13 +442,14 @@ int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, 
   if (split_ws && n < 2048 && n >= 512) {
     const int nk = (k + kBK - 1) / kBK;
     splits = (int)std::min<long long>(std::min(8, nk / 4), std::max<long long>(1, 148 / tiles));
-    const size_t need = (size_t)splits * tiles * kBM * plan.bn * 4 + (size_t)tiles * 4;
-    if (splits < 2 || need > split_ws_bytes) {
+    // tickets first, at a fixed place (they must stay zero between launches), then the partials
+    const size_t tickets_bytes = 65536;
+    const size_t need = tickets_bytes + (size_t)splits * tiles * kBM * plan.bn * 4;
+    if (splits < 2 || need > split_ws_bytes || (size_t)tiles * 4 > tickets_bytes) {
       splits = 1;
     } else {
-      part = static_cast<float *>(split_ws);
-      const size_t part_bytes = (size_t)splits * tiles * kBM * plan.bn * 4;
-      tickets = reinterpret_cast<unsigned *>(static_cast<char *>(split_ws) + part_bytes);
+      tickets = static_cast<unsigned *>(split_ws);
+      part = reinterpret_cast<float *>(static_cast<char *>(split_ws) + tickets_bytes);
     }
   }
   switch (plan.bn) {
