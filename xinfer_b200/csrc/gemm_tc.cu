@@ -380,10 +380,11 @@ int launch(const Plan &p, int m, int n, int k, void *out, long long ldo, unsigne
 }
 
 // The tile width whose tiles need the fewest waves over the SMs (time ~ waves x width; the wider
-// on ties); narrow outputs (512 <= N < 2048, long K) take 128-wide tiles split over K when a
-// split-K workspace is given, else (and below 512) 64-wide tiles for more CTAs.
-int choose_bn(int m, int n, int sms, bool split) {
-  if (n < 2048) return split && n >= 512 ? 128 : 64;
+// on ties); narrow outputs over long K (512 <= N < 2048, K >= 2048: out_proj, o_proj, down) take
+// 128-wide tiles split over K when a split-K workspace is given, other narrow outputs 64-wide
+// tiles for more CTAs.
+int choose_bn(int m, int n, int k, int sms, bool split) {
+  if (n < 2048) return split && n >= 512 && k >= 32 * kBK ? 128 : 64;
   const int widths[3] = {256, 128, 64};
   int best = 256;
   long long best_cost = -1;
@@ -427,7 +428,7 @@ int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, 
   if (!found) {
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    plan.bn = choose_bn(m, n, sms, split_ws != nullptr);
+    plan.bn = choose_bn(m, n, k, sms, split_ws != nullptr);
     if (!make_map(&plan.mx, x, m, k, kBM) || !make_map(&plan.mw, w, n, k, plan.bn))
       return xb::fail(XB_ERR_CUDA, "GEMM: tensor map creation failed");
     std::lock_guard<std::mutex> lock(plan_mu);
@@ -439,8 +440,8 @@ int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, 
   float *part = nullptr;
   unsigned *tickets = nullptr;
   const long long tiles = (long long)((n + plan.bn - 1) / plan.bn) * ((m + kBM - 1) / kBM);
-  if (split_ws && n < 2048 && n >= 512) {
-    const int nk = (k + kBK - 1) / kBK;
+  const int nk = (k + kBK - 1) / kBK;
+  if (split_ws && n < 2048 && n >= 512 && nk >= 32) {
     splits = (int)std::min<long long>(std::min(8, nk / 4), std::max<long long>(1, 148 / tiles));
     // tickets first, at a fixed place (they must stay zero between launches), then the partials
     const size_t tickets_bytes = 65536;
