@@ -339,7 +339,7 @@ bool make_map(CUtensorMap *map, const void *ptr, long long rows, long long cols,
 }
 
 struct PlanKey {
-  int m, n, k, device;
+  int m, n, k, device, split;  // split: a split-K workspace was given (it decides the tile width)
   long long ldo;
   const void *x, *w;
   void *out;
@@ -417,7 +417,8 @@ int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, 
   if (cudaGetDevice(&device) != cudaSuccess) return xb::fail(XB_ERR_CUDA, "GEMM: no current device");
   PlanKey key;
   std::memset(&key, 0, sizeof(key));
-  key.m = m; key.n = n; key.k = k; key.device = device; key.ldo = ldo; key.x = x; key.w = w; key.out = out;
+  key.m = m; key.n = n; key.k = k; key.device = device; key.split = split_ws != nullptr;
+  key.ldo = ldo; key.x = x; key.w = w; key.out = out;
   Plan plan;
   bool found = false;
   {
