@@ -59,6 +59,8 @@ static Layout layout(const XbGeometry &g, int T) {
   const int widest = std::max({g.hidden, g.intermediate, g.num_q_heads * g.head_dim, HVD});
   size_t off = kCtlBytes;
   auto take = [&](size_t bytes) { size_t o = off; off += (bytes + 255) & ~size_t(255); return o; };
+  // first, at an offset that does not depend on T: the split-K tickets must stay zero between calls
+  L.gsplit = take(xb::kGemmSplitBytes);
   L.h = take((size_t)T * g.hidden * 2);
   L.x = take((size_t)T * widest * 2);
   L.x2 = take((size_t)T * widest * 2);
@@ -76,7 +78,6 @@ static Layout layout(const XbGeometry &g, int T) {
   L.oatt = take((size_t)T * g.num_q_heads * g.head_dim * 2);
   L.xlast = take((size_t)g.hidden * 2 + 16);
   L.amax = take(kArgmaxBlocks * 8);
-  L.gsplit = take(xb::kGemmSplitBytes);
   L.total = off;
   return L;
 }
