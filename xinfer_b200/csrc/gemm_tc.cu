@@ -3,8 +3,9 @@
 // with fp32 accumulation in tensor memory and one rounding to bf16, the rounding of the
 // reference's cuBLAS linears as lowered by Inductor (a bf16 nn.Linear).
 //
-// One CTA per 128 x BN output tile (BN = 64, 128 or 256), 192 threads in three roles:
-//   warp 0  TMA producer: 128 x 64 tiles of x and BN x 64 tiles of W (K-major, 128-byte swizzle)
+// One CTA per RM x BN output tile (BN = 64, 128 or 256; RM = 128, or 64 for narrow outputs, whose
+// MMA rows 64..127 are computed from stale shared memory and discarded), 192 threads in three roles:
+//   warp 0  TMA producer: RM x 64 tiles of x and BN x 64 tiles of W (K-major, 128-byte swizzle)
 //           into a ring of shared-memory stages, completion counted on the stage's mbarrier;
 //   warp 1  allocates BN columns of tensor memory; one lane issues four tcgen05.mma (M = 128,
 //           N = BN, K = 16, bf16 x bf16 -> fp32) per stage and frees the stage with
@@ -136,13 +137,10 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<const uint32_t *>(&v);
 }
 
-// Split-K (gridDim.z = S > 1): CTA z accumulates k-blocks [z nk / S, (z + 1) nk / S) and writes
-// its fp32 tile to part[z]; the CTA that arrives last at the tile's ticket (no waiting) adds the S
-// partial tiles in order z = 0..S-1, rounds once and stores, then resets the ticket.
-template <int BN>
+template <int BN, int RM>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w, int M, int N,
-                int K, __nv_bfloat16 *out, long long ldo, unsigned *err, float *part, unsigned *tickets) {
+                int K, __nv_bfloat16 *out, long long ldo, unsigned *err) {
   using S = Shape<BN>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *base = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -151,10 +149,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *accum = empty + S::kStages;
   unsigned *tmem_slot = reinterpret_cast<unsigned *>(accum + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
-  const int nk_all = (K + kBK - 1) / kBK, nsplit = gridDim.z;
-  const int kb0 = (int)((long long)nk_all * blockIdx.z / nsplit);
-  const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / nsplit) - kb0;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * RM;
+  const int nk = (K + kBK - 1) / kBK;
+  constexpr unsigned kTxBytes = (RM + BN) * kBK * 2;  // bytes the two TMA loads of a stage bring
   if (!err) err = &g_error;
 
   if (threadIdx.x == 0) {
@@ -183,9 +180,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (kb >= S::kStages) mbar_wait(&empty[s], ((kb / S::kStages) - 1) & 1, err);
         unsigned char *a = base + s * S::kStageBytes;
         unsigned char *b = a + kBM * kBK * 2;
-        mbar_expect_tx(&full[s], S::kStageBytes);
-        tma_load_2d(a, &map_x, (kb0 + kb) * kBK, m0, &full[s]);
-        tma_load_2d(b, &map_w, (kb0 + kb) * kBK, n0, &full[s]);
+        mbar_expect_tx(&full[s], kTxBytes);
+        tma_load_2d(a, &map_x, kb * kBK, m0, &full[s]);
+        tma_load_2d(b, &map_w, kb * kBK, n0, &full[s]);
       }
     }
   } else if (warp == 1) {
@@ -209,65 +206,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     mbar_wait(accum, 0, err);
     tmem_fence_after();
-    const int row = m0 + quarter * 32 + lane;
-    auto store = [&](int c, const float *v) {
-      if (row >= M) return;
-      __nv_bfloat16 *dst = out + (long long)row * ldo + n0 + c;
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (n0 + c + 8 * q < N) {
-          uint4 u;
-          u.x = pack_bf16(v[8 * q + 0], v[8 * q + 1]);
-          u.y = pack_bf16(v[8 * q + 2], v[8 * q + 3]);
-          u.z = pack_bf16(v[8 * q + 4], v[8 * q + 5]);
-          u.w = pack_bf16(v[8 * q + 6], v[8 * q + 7]);
-          *reinterpret_cast<uint4 *>(dst + 8 * q) = u;
-        }
-    };
-    // partial tile z: [row within tile][column], BN fp32 per row
-    const long long tile = (long long)blockIdx.y * gridDim.x + blockIdx.x;
-    auto slot = [&](int z) {
-      return part + (((long long)z * gridDim.x * gridDim.y + tile) * kBM + quarter * 32 + lane) * BN;
-    };
+    const int trow = quarter * 32 + lane, row = m0 + trow;
+    if (trow < RM) {
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      uint32_t r[32];
-      tmem_ld32(tmem + ((unsigned)(quarter * 32) << 16) + c, r);
-      float v[32];
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((unsigned)(quarter * 32) << 16) + c, r);
+        if (row < M) {
+          __nv_bfloat16 *dst = out + (long long)row * ldo + n0 + c;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-      if (nsplit == 1) {
-        store(c, v);
-      } else {
-        float4 *dst = reinterpret_cast<float4 *>(slot(blockIdx.z) + c);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-      }
-    }
-    if (nsplit > 1) {
-      __shared__ unsigned last;
-      __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (threadIdx.x == 64) last = atomicAdd(&tickets[tile], 1u) == (unsigned)nsplit - 1;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (last) {
-        __threadfence();
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.f;
-          for (int z = 0; z < nsplit; ++z) {
-            const float4 *src = reinterpret_cast<const float4 *>(slot(z) + c);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float4 f = __ldcg(src + i);
-              v[4 * i] += f.x; v[4 * i + 1] += f.y; v[4 * i + 2] += f.z; v[4 * i + 3] += f.w;
+          for (int q = 0; q < 4; ++q)
+            if (n0 + c + 8 * q < N) {
+              uint4 v;
+              v.x = pack_bf16(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
+              v.y = pack_bf16(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
+              v.z = pack_bf16(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
+              v.w = pack_bf16(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
+              *reinterpret_cast<uint4 *>(dst + 8 * q) = v;
             }
-          }
-          store(c, v);
         }
-        if (threadIdx.x == 64) tickets[tile] = 0;
       }
     }
   }
@@ -339,7 +296,7 @@ bool make_map(CUtensorMap *map, const void *ptr, long long rows, long long cols,
 }
 
 struct PlanKey {
-  int m, n, k, device, split;  // split: a split-K workspace was given (it decides the tile width)
+  int m, n, k, device;
   long long ldo;
   const void *x, *w;
   void *out;
@@ -355,7 +312,7 @@ struct PlanHash {
 };
 struct Plan {
   CUtensorMap mx, mw;
-  int bn;
+  int bn, rm;  // tile width (weight rows) and height (token rows)
 };
 // Tensor maps of every (shape, operands, device) seen: a prefill chunk runs the same GEMMs on the
 // same buffers again and again.
@@ -363,28 +320,27 @@ constexpr size_t kMaxPlans = 4096;
 std::mutex plan_mu;
 std::unordered_map<PlanKey, Plan, PlanHash> plans;
 
-template <int BN>
-int launch(const Plan &p, int m, int n, int k, void *out, long long ldo, unsigned *err, int splits, float *part,
-           unsigned *tickets, cudaStream_t st) {
+template <int BN, int RM>
+int launch(const Plan &p, int m, int n, int k, void *out, long long ldo, unsigned *err, cudaStream_t st) {
   static std::once_flag attr;
   static cudaError_t attr_rc = cudaSuccess;
   std::call_once(attr, [] {
-    attr_rc = cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape<BN>::kSmem);
+    attr_rc = cudaFuncSetAttribute(gemm_kernel<BN, RM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   Shape<BN>::kSmem);
   });
   if (attr_rc != cudaSuccess) return xb::fail(XB_ERR_CUDA, std::string("GEMM: ") + cudaGetErrorString(attr_rc));
-  const dim3 grid((n + BN - 1) / BN, (m + kBM - 1) / kBM, splits);
-  gemm_kernel<BN><<<grid, kThreads, Shape<BN>::kSmem, st>>>(p.mx, p.mw, m, n, k, static_cast<__nv_bfloat16 *>(out),
-                                                             ldo, err, part, tickets);
+  const dim3 grid((n + BN - 1) / BN, (m + RM - 1) / RM);
+  gemm_kernel<BN, RM><<<grid, kThreads, Shape<BN>::kSmem, st>>>(p.mx, p.mw, m, n, k,
+                                                                 static_cast<__nv_bfloat16 *>(out), ldo, err);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? XB_OK : xb::fail(XB_ERR_CUDA, std::string("GEMM launch: ") + cudaGetErrorString(e));
 }
 
 // The tile width whose tiles need the fewest waves over the SMs (time ~ waves x width; the wider
-// on ties); narrow outputs over long K (512 <= N < 2048, K >= 2048: out_proj, o_proj, down) take
-// 128-wide tiles split over K when a split-K workspace is given, other narrow outputs 64-wide
-// tiles for more CTAs.
-int choose_bn(int m, int n, int k, int sms, bool split) {
-  if (n < 2048) return split && n >= 512 && k >= 32 * kBK ? 128 : 64;
+// on ties); narrow outputs (N < 2048: out_proj, o_proj, down of the small models) take 64 x 64
+// tiles, twice the CTAs of 128-row tiles with half the operand bytes each.
+int choose_bn(int m, int n, int sms) {
+  if (n < 2048) return 64;
   const int widths[3] = {256, 128, 64};
   int best = 256;
   long long best_cost = -1;
@@ -395,11 +351,12 @@ int choose_bn(int m, int n, int k, int sms, bool split) {
   }
   return best;
 }
+int rows_per_tile(int n) { return n < 2048 ? 64 : kBM; }
 
 } // namespace xbtc
 
 int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, long long ldo, void *stream,
-                  unsigned *err, void *split_ws, size_t split_ws_bytes) {
+                  unsigned *err) {
   using namespace xbtc;
   if (m < 1 || n < 1 || k < 1 || !x || !w || !out || ldo < n) return xb::fail(XB_ERR_INVALID, "invalid GEMM arguments");
   if (k % 8) return xb::fail(XB_ERR_INVALID, "GEMM K must be a multiple of 8");
@@ -417,7 +374,7 @@ int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, 
   if (cudaGetDevice(&device) != cudaSuccess) return xb::fail(XB_ERR_CUDA, "GEMM: no current device");
   PlanKey key;
   std::memset(&key, 0, sizeof(key));
-  key.m = m; key.n = n; key.k = k; key.device = device; key.split = split_ws != nullptr;
+  key.m = m; key.n = n; key.k = k; key.device = device;
   key.ldo = ldo; key.x = x; key.w = w; key.out = out;
   Plan plan;
   bool found = false;
@@ -429,39 +386,23 @@ int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, 
   if (!found) {
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    plan.bn = choose_bn(m, n, k, sms, split_ws != nullptr);
-    if (!make_map(&plan.mx, x, m, k, kBM) || !make_map(&plan.mw, w, n, k, plan.bn))
+    plan.bn = choose_bn(m, n, sms);
+    plan.rm = rows_per_tile(n);
+    if (!make_map(&plan.mx, x, m, k, plan.rm) || !make_map(&plan.mw, w, n, k, plan.bn))
       return xb::fail(XB_ERR_CUDA, "GEMM: tensor map creation failed");
     std::lock_guard<std::mutex> lock(plan_mu);
     if (plans.size() >= kMaxPlans) plans.clear();
     plans.emplace(key, plan);
   }
-  // narrow outputs: split K so that about one CTA per SM streams K / S of the operands
-  int splits = 1;
-  float *part = nullptr;
-  unsigned *tickets = nullptr;
-  const long long tiles = (long long)((n + plan.bn - 1) / plan.bn) * ((m + kBM - 1) / kBM);
-  const int nk = (k + kBK - 1) / kBK;
-  if (split_ws && n < 2048 && n >= 512 && nk >= 32) {
-    splits = (int)std::min<long long>(std::min(8, nk / 4), std::max<long long>(1, 148 / tiles));
-    // tickets first, at a fixed place (they must stay zero between launches), then the partials
-    const size_t tickets_bytes = 65536;
-    const size_t need = tickets_bytes + (size_t)splits * tiles * kBM * plan.bn * 4;
-    if (splits < 2 || need > split_ws_bytes || (size_t)tiles * 4 > tickets_bytes) {
-      splits = 1;
-    } else {
-      tickets = static_cast<unsigned *>(split_ws);
-      part = reinterpret_cast<float *>(static_cast<char *>(split_ws) + tickets_bytes);
-    }
-  }
+  if (plan.rm == 64) return launch<64, 64>(plan, m, n, k, out, ldo, err, st);
   switch (plan.bn) {
-    case 256: return launch<256>(plan, m, n, k, out, ldo, err, splits, part, tickets, st);
-    case 128: return launch<128>(plan, m, n, k, out, ldo, err, splits, part, tickets, st);
-    default: return launch<64>(plan, m, n, k, out, ldo, err, splits, part, tickets, st);
+    case 256: return launch<256, kBM>(plan, m, n, k, out, ldo, err, st);
+    case 128: return launch<128, kBM>(plan, m, n, k, out, ldo, err, st);
+    default: return launch<64, kBM>(plan, m, n, k, out, ldo, err, st);
   }
 }
 
 extern "C" int xb_gemm_bf16(int32_t m, int32_t n, int32_t k, const void *x, const void *w, void *out,
                             void *stream) {
-  return xb::gemm_bf16(m, n, k, x, w, out, n, stream, nullptr, nullptr, 0);
+  return xb::gemm_bf16(m, n, k, x, w, out, n, stream, nullptr);
 }

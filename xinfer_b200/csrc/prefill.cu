@@ -37,7 +37,7 @@ constexpr int kCtlBytes = 1024;
 enum { PERR_TOKEN = 4 };
 
 struct Layout {
-  size_t h, x, x2, out, proj, qn, kn, vv, beta, glog, rec, core, qatt, oatt, xlast, amax, gsplit, total;
+  size_t h, x, x2, out, proj, qn, kn, vv, beta, glog, rec, core, qatt, oatt, xlast, amax, total;
 };
 
 static int lin_channels(const XbGeometry &g) { return (2 * g.lin_key_heads + g.lin_value_heads) * g.lin_head_dim; }
@@ -59,8 +59,6 @@ static Layout layout(const XbGeometry &g, int T) {
   const int widest = std::max({g.hidden, g.intermediate, g.num_q_heads * g.head_dim, HVD});
   size_t off = kCtlBytes;
   auto take = [&](size_t bytes) { size_t o = off; off += (bytes + 255) & ~size_t(255); return o; };
-  // first, at an offset that does not depend on T: the split-K tickets must stay zero between calls
-  L.gsplit = take(xb::kGemmSplitBytes);
   L.h = take((size_t)T * g.hidden * 2);
   L.x = take((size_t)T * widest * 2);
   L.x2 = take((size_t)T * widest * 2);
@@ -693,7 +691,6 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
     cudaError_t e_ = cudaGetLastError();                                                             \
     if (e_ != cudaSuccess) return xb::fail(XB_ERR_CUDA, std::string("prefill launch: ") + cudaGetErrorString(e_)); \
   } while (0)
-  void *gsplit = ws + L.gsplit;  // split-K partials of the narrow GEMMs
   const int NP = proj_width(g);
   if (NP % 4) return xb::fail(XB_ERR_UNSUPPORTED, "prefill needs projection rows of a multiple of 4 elements");
   bf16 *proj = P(L.proj);
@@ -710,11 +707,10 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
       rows += p.rows;
       prev = &p;
     }
-    if (packed)
-      return xb::gemm_bf16(T, rows, k, xin, parts.begin()->w, proj, NP, stream, err, gsplit, xb::kGemmSplitBytes);
+    if (packed) return xb::gemm_bf16(T, rows, k, xin, parts.begin()->w, proj, NP, stream, err);
     int col = 0;
     for (const Part &p : parts) {
-      const int rc = xb::gemm_bf16(T, p.rows, k, xin, p.w, proj + col, NP, stream, err, gsplit, xb::kGemmSplitBytes);
+      const int rc = xb::gemm_bf16(T, p.rows, k, xin, p.w, proj + col, NP, stream, err);
       if (rc) return rc;
       col += p.rows;
     }
@@ -753,7 +749,7 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
                                                                               (const bf16 *)w.gnorm, x2, HV, T,
                                                                               g.rms_eps);
       XB_LAUNCHED();
-      XB_TRY(xb::gemm_bf16(T, H, HVD, x2, w.out_proj, out, H, stream, err, gsplit, xb::kGemmSplitBytes));
+      XB_TRY(xb::gemm_bf16(T, H, HVD, x2, w.out_proj, out, H, stream, err));
     } else {
       const int qrows = HQ * D * (q35 ? 2 : 1);
       XB_TRY(group(x, H, {{w.q_proj, qrows}, {w.k_proj, HKV * D}, {w.v_proj, HKV * D}}));
@@ -780,14 +776,14 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
       XB_TRY(xb_prefix_attention(&at, stream));
       attn_out_kernel<<<dim3(T, HQ), 128, 0, st>>>(P(L.oatt), qo, NP, x2, HQ, D, T, q35);
       XB_LAUNCHED();
-      XB_TRY(xb::gemm_bf16(T, H, HQ * D, x2, w.o_proj, out, H, stream, err, gsplit, xb::kGemmSplitBytes));
+      XB_TRY(xb::gemm_bf16(T, H, HQ * D, x2, w.o_proj, out, H, stream, err));
     }
     add_rmsnorm_kernel<<<T, rn, 0, st>>>(h, out, (const bf16 *)w.post_norm, x, H, g.rms_eps, q35, 0);
     XB_LAUNCHED();
     XB_TRY(group(x, H, {{w.gate, I}, {w.up, I}}));
     silu_mul_kernel<<<(unsigned)(((long long)T * (I / 8) + 255) / 256), 256, 0, st>>>(proj, x2, I, NP, T);
     XB_LAUNCHED();
-    XB_TRY(xb::gemm_bf16(T, H, I, x2, w.down, out, H, stream, err, gsplit, xb::kGemmSplitBytes));
+    XB_TRY(xb::gemm_bf16(T, H, I, x2, w.down, out, H, stream, err));
     if (l + 1 < g.num_layers) {
       add_rmsnorm_kernel<<<T, rn, 0, st>>>(h, out, (const bf16 *)model->w.layers[l + 1].input_norm, x, H,
                                             g.rms_eps, q35, 0);
@@ -798,8 +794,7 @@ extern "C" int xb_prefill_step(const XbModel *model, const XbPrefillArgs *a, voi
     }
     XB_LAUNCHED();
   }
-  XB_TRY(xb::gemm_bf16(1, g.vocab, H, P(L.xlast), model->w.lm_head, a->logits, g.vocab, stream, err, gsplit,
-                       xb::kGemmSplitBytes));
+  XB_TRY(xb::gemm_bf16(1, g.vocab, H, P(L.xlast), model->w.lm_head, a->logits, g.vocab, stream, err));
   if (a->next_token) {
     argmax_partial_kernel<<<kArgmaxBlocks, 256, 0, st>>>((const bf16 *)a->logits, g.vocab, F(L.amax),
                                                          (int *)(ws + L.amax) + kArgmaxBlocks);

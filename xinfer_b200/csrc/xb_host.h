@@ -24,9 +24,6 @@ int fail(int code, const std::string &msg);
 // out[m, n] (rows ldo elements apart) = x[m, k] . w[n, k]^T in bf16 with fp32 accumulation
 // (gemm_tc.cu); xb_gemm_bf16 is the packed case ldo = n. A device-side wait that expired sets
 // bit 0 of *err (a library-wide word when err is null).
-// With `split_ws` (zeroed once, kGemmSplitBytes), narrow outputs are split over K.
 int gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, long long ldo, void *stream,
-              unsigned *err, void *split_ws, size_t split_ws_bytes);
-// split-K workspace of gemm_bf16: fp32 partial tiles for one wave of CTAs, and their tickets
-constexpr size_t kGemmSplitBytes = (size_t)148 * 128 * 128 * 4 + 65536;
+              unsigned *err);
 } // namespace xb
