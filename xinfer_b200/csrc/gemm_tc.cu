@@ -35,10 +35,15 @@ enum { GERR_WAIT = 1 };
 
 __device__ unsigned g_error;  // error word of launches that were given none
 
-template <int BN> struct Shape {
-  static constexpr int kStageBytes = (kBM + BN) * kBK * 2;
-  static constexpr int kStages = BN == 256 ? 4 : BN == 128 ? 6 : 8;
-  static constexpr int kSmem = kStages * kStageBytes + 1024 /* alignment */ + 256 /* barriers */;
+// A stage holds RM rows of x then BN rows of W, 128 bytes each (64 bf16 of K). With RM = 64 the
+// 128-row MMA operand A runs on into the W rows: its upper half is discarded. As many stages as
+// fit in 227 KB of shared memory: the bytes in flight set the streaming rate.
+template <int BN, int RM> struct Shape {
+  static constexpr int kStageBytes = (RM + BN) * kBK * 2;
+  static constexpr int kSmemMax = 227 * 1024, kExtra = 1024 /* alignment */ + 512 /* barriers */;
+  static constexpr int kStages = (kSmemMax - kExtra) / kStageBytes < 16 ? (kSmemMax - kExtra) / kStageBytes : 16;
+  static constexpr int kSmem = kStages * kStageBytes + kExtra;
+  static_assert(kStages >= 2 && kBM * kBK * 2 <= kStageBytes, "stage layout");
 };
 
 __device__ __forceinline__ unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
@@ -141,7 +146,7 @@ template <int BN, int RM>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w, int M, int N,
                 int K, __nv_bfloat16 *out, long long ldo, unsigned *err) {
-  using S = Shape<BN>;
+  using S = Shape<BN, RM>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *base = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t *full = reinterpret_cast<uint64_t *>(base + S::kStages * S::kStageBytes);
@@ -179,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = kb % S::kStages;
         if (kb >= S::kStages) mbar_wait(&empty[s], ((kb / S::kStages) - 1) & 1, err);
         unsigned char *a = base + s * S::kStageBytes;
-        unsigned char *b = a + kBM * kBK * 2;
+        unsigned char *b = a + RM * kBK * 2;
         mbar_expect_tx(&full[s], kTxBytes);
         tma_load_2d(a, &map_x, kb * kBK, m0, &full[s]);
         tma_load_2d(b, &map_w, kb * kBK, n0, &full[s]);
@@ -193,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(&full[s], (kb / S::kStages) & 1, err);
         tmem_fence_after();
         const unsigned a = smem_u32(base + s * S::kStageBytes);
-        const unsigned b = a + kBM * kBK * 2;
+        const unsigned b = a + RM * kBK * 2;
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
           mma_bf16(tmem, smem_desc(a + kk * 32), smem_desc(b + kk * 32), idesc, (kb | kk) != 0);
@@ -326,32 +331,33 @@ int launch(const Plan &p, int m, int n, int k, void *out, long long ldo, unsigne
   static cudaError_t attr_rc = cudaSuccess;
   std::call_once(attr, [] {
     attr_rc = cudaFuncSetAttribute(gemm_kernel<BN, RM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   Shape<BN>::kSmem);
+                                   Shape<BN, RM>::kSmem);
   });
   if (attr_rc != cudaSuccess) return xb::fail(XB_ERR_CUDA, std::string("GEMM: ") + cudaGetErrorString(attr_rc));
   const dim3 grid((n + BN - 1) / BN, (m + RM - 1) / RM);
-  gemm_kernel<BN, RM><<<grid, kThreads, Shape<BN>::kSmem, st>>>(p.mx, p.mw, m, n, k,
+  gemm_kernel<BN, RM><<<grid, kThreads, Shape<BN, RM>::kSmem, st>>>(p.mx, p.mw, m, n, k,
                                                                  static_cast<__nv_bfloat16 *>(out), ldo, err);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? XB_OK : xb::fail(XB_ERR_CUDA, std::string("GEMM launch: ") + cudaGetErrorString(e));
 }
 
-// The tile width whose tiles need the fewest waves over the SMs (time ~ waves x width; the wider
-// on ties); narrow outputs (N < 2048: out_proj, o_proj, down of the small models) take 64 x 64
-// tiles, twice the CTAs of 128-row tiles with half the operand bytes each.
-int choose_bn(int m, int n, int sms) {
+// Tile height: 64 rows for a few tokens (the last token's lm_head) and for narrow outputs
+// (N < 2048: out_proj, o_proj, down of the small models; twice the CTAs of 128-row tiles), else 128.
+int rows_per_tile(int m, int n) { return m <= 64 || n < 2048 ? 64 : kBM; }
+// Tile width: 64 for narrow outputs, else the one whose tiles need the fewest waves over the SMs
+// (time ~ waves x width; the wider on ties).
+int choose_bn(int m, int n, int rm, int sms) {
   if (n < 2048) return 64;
   const int widths[3] = {256, 128, 64};
   int best = 256;
   long long best_cost = -1;
   for (int w : widths) {
-    const long long tiles = (long long)((m + kBM - 1) / kBM) * ((n + w - 1) / w);
+    const long long tiles = (long long)((m + rm - 1) / rm) * ((n + w - 1) / w);
     const long long cost = (tiles + sms - 1) / sms * w;
     if (best_cost < 0 || cost < best_cost) { best = w; best_cost = cost; }
   }
   return best;
 }
-int rows_per_tile(int n) { return n < 2048 ? 64 : kBM; }
 
 } // namespace xbtc
 
@@ -386,15 +392,21 @@ int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, 
   if (!found) {
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    plan.bn = choose_bn(m, n, sms);
-    plan.rm = rows_per_tile(n);
+    plan.rm = rows_per_tile(m, n);
+    plan.bn = choose_bn(m, n, plan.rm, sms);
     if (!make_map(&plan.mx, x, m, k, plan.rm) || !make_map(&plan.mw, w, n, k, plan.bn))
       return xb::fail(XB_ERR_CUDA, "GEMM: tensor map creation failed");
     std::lock_guard<std::mutex> lock(plan_mu);
     if (plans.size() >= kMaxPlans) plans.clear();
     plans.emplace(key, plan);
   }
-  if (plan.rm == 64) return launch<64, 64>(plan, m, n, k, out, ldo, err, st);
+  if (plan.rm == 64) {
+    switch (plan.bn) {
+      case 256: return launch<256, 64>(plan, m, n, k, out, ldo, err, st);
+      case 128: return launch<128, 64>(plan, m, n, k, out, ldo, err, st);
+      default: return launch<64, 64>(plan, m, n, k, out, ldo, err, st);
+    }
+  }
   switch (plan.bn) {
     case 256: return launch<256, kBM>(plan, m, n, k, out, ldo, err, st);
     case 128: return launch<128, kBM>(plan, m, n, k, out, ldo, err, st);
