@@ -345,7 +345,8 @@ int launch(const Plan &p, int m, int n, int k, void *out, long long ldo, unsigne
 // (N < 2048: out_proj, o_proj, down of the small models; twice the CTAs of 128-row tiles), else 128.
 int rows_per_tile(int m, int n) { return m <= 64 || n < 2048 ? 64 : kBM; }
 // Tile width: 64 for narrow outputs, else the one whose tiles need the fewest waves over the SMs
-// (time ~ waves x width; the wider on ties).
+// weighted by the bytes a tile streams per K step (time ~ waves x (rows + width); the wider on
+// ties).
 int choose_bn(int m, int n, int rm, int sms) {
   if (n < 2048) return 64;
   const int widths[3] = {256, 128, 64};
@@ -353,7 +354,7 @@ int choose_bn(int m, int n, int rm, int sms) {
   long long best_cost = -1;
   for (int w : widths) {
     const long long tiles = (long long)((m + rm - 1) / rm) * ((n + w - 1) / w);
-    const long long cost = (tiles + sms - 1) / sms * w;
+    const long long cost = (tiles + sms - 1) / sms * (rm + w);
     if (best_cost < 0 || cost < best_cost) { best = w; best_cost = cost; }
   }
   return best;
