@@ -325,15 +325,17 @@ constexpr size_t kMaxPlans = 4096;
 std::mutex plan_mu;
 std::unordered_map<PlanKey, Plan, PlanHash> plans;
 
+// the kernel's shared-memory allowance on the current device (set when a plan is made)
+template <int BN, int RM> cudaError_t allow_smem() {
+  return cudaFuncSetAttribute(gemm_kernel<BN, RM>, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape<BN, RM>::kSmem);
+}
+cudaError_t allow_smem(int bn, int rm) {
+  if (rm == 64) return bn == 256 ? allow_smem<256, 64>() : bn == 128 ? allow_smem<128, 64>() : allow_smem<64, 64>();
+  return bn == 256 ? allow_smem<256, kBM>() : bn == 128 ? allow_smem<128, kBM>() : allow_smem<64, kBM>();
+}
+
 template <int BN, int RM>
 int launch(const Plan &p, int m, int n, int k, void *out, long long ldo, unsigned *err, cudaStream_t st) {
-  static std::once_flag attr;
-  static cudaError_t attr_rc = cudaSuccess;
-  std::call_once(attr, [] {
-    attr_rc = cudaFuncSetAttribute(gemm_kernel<BN, RM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   Shape<BN, RM>::kSmem);
-  });
-  if (attr_rc != cudaSuccess) return xb::fail(XB_ERR_CUDA, std::string("GEMM: ") + cudaGetErrorString(attr_rc));
   const dim3 grid((n + BN - 1) / BN, (m + RM - 1) / RM);
   gemm_kernel<BN, RM><<<grid, kThreads, Shape<BN, RM>::kSmem, st>>>(p.mx, p.mw, m, n, k,
                                                                  static_cast<__nv_bfloat16 *>(out), ldo, err);
@@ -397,6 +399,8 @@ int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, 
     plan.bn = choose_bn(m, n, plan.rm, sms);
     if (!make_map(&plan.mx, x, m, k, plan.rm) || !make_map(&plan.mw, w, n, k, plan.bn))
       return xb::fail(XB_ERR_CUDA, "GEMM: tensor map creation failed");
+    const cudaError_t e = allow_smem(plan.bn, plan.rm);
+    if (e != cudaSuccess) return xb::fail(XB_ERR_CUDA, std::string("GEMM: ") + cudaGetErrorString(e));
     std::lock_guard<std::mutex> lock(plan_mu);
     if (plans.size() >= kMaxPlans) plans.clear();
     plans.emplace(key, plan);
