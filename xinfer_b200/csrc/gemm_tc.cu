@@ -180,6 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_x)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % S::kStages;
         if (kb >= S::kStages) mbar_wait(&empty[s], ((kb / S::kStages) - 1) & 1, err);
