@@ -1423,6 +1423,150 @@ template <int NB> struct Consumer {
   // ---- Gated DeltaNet recurrent step (compiler/qwen35/kernels/recurrent.py:20-124) ---------
   // Work item = (row b, value head h, 16-column tile t of the 128x128 state). The state slice,
   // conv windows and taps are loaded up front; the projections of this head are polled.
+#if XB_TENSOR_TILES
+  // ---- Gated DeltaNet, batch rows 4-8: one work item per (row, value head) ------------------
+  // The q/k conv and l2-norms run once per head instead of once per 16-column tile. The head's
+  // 128 x 128 fp32 state is updated in four passes of 32 columns: thread t keeps column t & 31 of
+  // the pass, rows 16 (t >> 5) .. + 15, and the eight row groups are added in shared memory.
+  // Outputs as the per-tile items: the core values, the per-16-column sums of squares for the
+  // gated norm, the updated state.
+  __device__ __forceinline__ void delta(int l) {
+    stage_begin();
+    const XbLayerWeights &w = p.layers[l];
+    const unsigned tg = tag(l, 0);
+    const int HK = p.HK, HV = p.HV, DK = p.DK;
+    const int CH = (2 * HK + HV) * DK, CW = p.CW;
+    const int group = HV / HK;
+    const int items = p.B * HV;
+    const bf16 *cw = (const bf16 *)w.conv_w;
+    float *qk = red;          // [2 DK]  (q | k)
+    float *vv = red + 256;    // [DK]
+    float *pn = red + 384;    // [kWarps] norm partials
+    float *gt = red + 392;    // beta, decay
+    float *pp = red + 400;    // [8][32] prediction partials
+    float *po = red + 656;    // [8][32] output partials
+    const bf16 *conv_in_all = (const bf16 *)p.sa[l];
+    const float *rec_in_all = (const float *)p.sb[l];
+    float *rec_out_all = (float *)p.sd[l];
+    const int c32 = tid & 31, rg = tid >> 5, r0 = rg * 16;
+    for (int item = blockIdx.x; item < items; item += p.ncta) {
+      const int b = item / HV;
+      const int h = item % HV;
+      const int kh = h / group;
+      const float *S_in = rec_in_all + (((size_t)b * HV + h) * DK) * DK;
+      float *S_out = rec_out_all + (((size_t)b * HV + h) * DK) * DK;
+      unsigned *core = p.core + (size_t)b * HV * DK + h * DK;
+      u64 *ssq = p.ssq + ((size_t)b * HV + h) * 8;
+      if (p.q_len[b] == 0) {
+        // Empty row: replacement state equals the input state (a no-op when in place).
+        for (int i = tid; i < DK * DK; i += kCT) S_out[i] = S_in[i];
+        if (tid < DK) core[tid] = tagged(0.f, tg);
+        if (tid < 8) st_u64(ssq + tid, ftag(0.f, tg));
+        continue;
+      }
+      const bf16 *cin = conv_in_all + (size_t)b * CH * CW;
+      const unsigned *x = p.proj + (size_t)b * p.pstride;
+      // conv channels: q (tid < 128) or k (tid >= 128) of key head kh; v channel tid (< 128)
+      const int chq = tid < DK ? kh * DK + tid : (HK + kh) * DK + (tid - DK);
+      const int chv = (2 * HK + h) * DK + (tid & 127);
+      const uint2 cq = *reinterpret_cast<const uint2 *>(cin + (size_t)chq * CW);
+      const uint2 wq = *reinterpret_cast<const uint2 *>(cw + (size_t)chq * CW);
+      uint2 cv = make_uint2(0, 0), wvv = make_uint2(0, 0);
+      if (tid < DK) {
+        cv = *reinterpret_cast<const uint2 *>(cin + (size_t)chv * CW);
+        wvv = *reinterpret_cast<const uint2 *>(cw + (size_t)chv * CW);
+      }
+      float gsc = 0.f;
+      if (warp == 0) {
+        if (lane == 2) gsc = bf(((const bf16 *)w.dt_bias)[h]);
+        else if (lane == 3) gsc = bf(((const bf16 *)w.a_log)[h]);
+      }
+      // q/k channel, v channel (tid < 128), then b and a (warp 0, lanes 0 and 1), polled together
+      unsigned xw[3];
+      auto xaddr = [&](int k) { return k == 0 ? x + chq : k == 1 ? x + chv : x + CH + HV * DK + lane * HV + h; };
+      auto xwant = [&](int k) { return k == 0 || (k == 1 && tid < DK) || (k == 2 && warp == 0 && lane < 2); };
+#pragma unroll
+      for (int k = 0; k < 3; ++k) xw[k] = xwant(k) ? ld_poll_u32(xaddr(k)) : 0u;
+      settle1(xw, xaddr, xwant, tg);
+      trace_mark(1);
+      const float xq = bf_lo(xw[0]);
+      const float xv = tid < DK ? bf_lo(xw[1]) : 0.f;
+      if (warp == 0 && lane < 2) gsc = bf_lo(xw[2]);  // b, a
+      // causal conv (width 4) over [conv[1..3], x] + SiLU, rounded as recurrent.py:32-58
+      auto conv = [](uint2 cs, uint2 ws, float xx) -> float {
+        float tot = 0.f;
+        tot = fmaf(bf_hi(cs.x), bf_lo(ws.x), tot);
+        tot = fmaf(bf_lo(cs.y), bf_hi(ws.x), tot);
+        tot = fmaf(bf_hi(cs.y), bf_lo(ws.y), tot);
+        tot = fmaf(xx, bf_hi(ws.y), tot);
+        const float v = rbf(tot);
+        return rbf(v * (1.f / (1.f + expf(-v))));
+      };
+      const float qkv_val = conv(cq, wq, xq);
+      qk[tid] = qkv_val;
+      if (tid < DK) vv[tid] = conv(cv, wvv, xv);
+      if (warp == 0) {
+        const float bb = __shfl_sync(0xffffffffu, gsc, 0);
+        const float aa = __shfl_sync(0xffffffffu, gsc, 1);
+        const float dt = __shfl_sync(0xffffffffu, gsc, 2);
+        const float al = __shfl_sync(0xffffffffu, gsc, 3);
+        if (lane == 0) {
+          gt[0] = rbf(1.f / (1.f + expf(-bb)));  // beta
+          const float xx = aa + dt;
+          const float sp = xx > 20.f ? xx : log1pf(expf(xx));
+          gt[1] = expf(-expf(al) * sp);          // decay = exp(g)
+        }
+      }
+      {
+        const float sq = warp_sum(qkv_val * qkv_val);
+        if (lane == 0) pn[warp] = sq;
+      }
+      csync();
+      const float qs = rsqrtf(pn[0] + pn[1] + pn[2] + pn[3] + 1e-6f);
+      const float ks = rsqrtf(pn[4] + pn[5] + pn[6] + pn[7] + 1e-6f);
+      const float beta = gt[0], decay = gt[1];
+#pragma unroll 1
+      for (int pass = 0; pass < 4; ++pass) {
+        const int col = pass * 32 + c32;
+        float S[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) S[i] = S_in[(size_t)(r0 + i) * DK + col];
+        float pr = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          S[i] *= decay;
+          pr = fmaf(S[i], qk[DK + r0 + i] * ks, pr);
+        }
+        pp[rg * 32 + c32] = pr;
+        csync();
+        float pred = 0.f;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) pred += pp[g * 32 + c32];
+        const float delta_c = (vv[col] - pred) * beta;
+        float o = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          S[i] = fmaf(qk[DK + r0 + i] * ks, delta_c, S[i]);
+          o = fmaf(S[i], qk[r0 + i] * qs * p.dk_scale, o);
+          S_out[(size_t)(r0 + i) * DK + col] = S[i];
+        }
+        po[rg * 32 + c32] = o;
+        csync();
+        if (tid < 32) {
+          float out = 0.f;
+#pragma unroll
+          for (int g = 0; g < 8; ++g) out += po[g * 32 + tid];
+          const float ob = rbf(out);
+          core[pass * 32 + tid] = tagged(ob, tg);
+          float sq = ob * ob;
+#pragma unroll
+          for (int o2 = 8; o2; o2 >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o2);
+          if ((tid & 15) == 0) st_u64(ssq + pass * 2 + (tid >> 4), ftag(sq, tg));
+        }
+      }
+    }
+  }
+#else
   __device__ __forceinline__ void delta(int l) {
     stage_begin();
     const XbLayerWeights &w = p.layers[l];
@@ -1565,6 +1709,8 @@ template <int NB> struct Consumer {
       }
     }
   }
+
+#endif
 
   // ---- attention: q/k norm, RoPE, KV append, split-KV partials ----------------------------
   // Work item = (row b, KV head, split of the populated prefix). Warp w serves query head
