@@ -1,6 +1,6 @@
 """The multi-GPU bench path on CPU: replicas, one process per rank, over a gloo group.
 
-Batch-1 decode does not shard (SURVEY's multi-GPU row is replicas only): each rank runs its own
+Batch-1 decode does not shard (multi-GPU means independent replicas): each rank runs its own
 model copy and the job reports the slowest rank's time for all ranks' tokens. These tests run
 that aggregation with world size 2 on the gloo backend, and the reference arm's rank rule.
 """
