@@ -38,7 +38,7 @@ def model(name, capacity, device):
 
 @pytest.mark.parametrize("m,n,k", [(1, 1024, 1024), (7, 8224, 1024), (128, 3584, 1024), (300, 1024, 3584),
                                    (512, 2048, 2560), (1, 151936, 1024), (513, 24, 64), (37, 5, 64),
-                                   (512, 2, 1024)])
+                                   (512, 2, 1024), (100, 2056, 1000), (65, 1032, 4104), (1, 248320, 1024)])
 def test_gemm_matches_fp32_product(m, n, k, cuda_device):
     torch.backends.cuda.matmul.allow_tf32 = False
     gen = torch.Generator(device=cuda_device).manual_seed(m * 7 + n)
