@@ -1874,10 +1874,8 @@ template <int NB> struct Consumer {
           if (e < EPL) sc = fmaf(q[e], kf[e], sc);
         sc = warp_sum(sc) * scale;
         const float mn = fmaxf(m, sc);
-        // the hardware exponential, as FlashAttention-2 computes its probabilities (exp2 of a
-        // log2(e)-scaled argument)
-        const float corr = __expf(m - mn);
-        const float pe = __expf(sc - mn);
+        const float corr = expf(m - mn);
+        const float pe = expf(sc - mn);
         lsum = lsum * corr + pe;
         // FlashAttention-2 rounding: the row sum over fp32 probabilities, P.V over bf16 ones
         const float pb = rbf(pe);
