@@ -40,7 +40,7 @@ __device__ unsigned g_error;  // error word of launches that were given none
 // fit in 227 KB of shared memory: the bytes in flight set the streaming rate.
 template <int BN, int RM> struct Shape {
   static constexpr int kStageBytes = (RM + BN) * kBK * 2;
-  static constexpr int kSmemMax = 227 * 1024, kExtra = 1024 /* alignment */ + 512 /* barriers */;
+  static constexpr int kSmemMax = 227 * 1024, kExtra = 1024 /* alignment */ + 512 /* barriers, flags */;
   static constexpr int kStages = (kSmemMax - kExtra) / kStageBytes < 16 ? (kSmemMax - kExtra) / kStageBytes : 16;
   static constexpr int kSmem = kStages * kStageBytes + kExtra;
   static_assert(kStages >= 2 && kBM * kBK * 2 <= kStageBytes, "stage layout");
@@ -70,13 +70,16 @@ __device__ __forceinline__ unsigned long long global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// bounded wait for the phase with the given parity; false (and the error word set) on expiry
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, unsigned *err) {
+// bounded wait for the phase with the given parity; false on expiry, which sets the error word
+// and the CTA's `broken` flag (later waits of the CTA then give up at once)
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, unsigned *err, volatile int *broken,
+                                          unsigned long long limit_ns = kWaitNs) {
   if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   while (!mbar_try(bar, parity))
-    if (global_ns() - t0 > kWaitNs) {
+    if (*broken || global_ns() - t0 > limit_ns) {
       atomicOr(err, (unsigned)GERR_WAIT);
+      *broken = 1;
       return false;
     }
   return true;
@@ -153,6 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *empty = full + S::kStages;
   uint64_t *accum = empty + S::kStages;
   unsigned *tmem_slot = reinterpret_cast<unsigned *>(accum + 1);
+  volatile int *broken = reinterpret_cast<volatile int *>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * RM;
   const int nk = (K + kBK - 1) / kBK;
@@ -165,6 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum, 1);
+    *broken = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {  // BN columns of tensor memory for the 128 x BN fp32 accumulator
@@ -184,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % S::kStages;
-        if (kb >= S::kStages) mbar_wait(&empty[s], ((kb / S::kStages) - 1) & 1, err);
+        if (kb >= S::kStages) mbar_wait(&empty[s], ((kb / S::kStages) - 1) & 1, err, broken);
         unsigned char *a = base + s * S::kStageBytes;
         unsigned char *b = a + RM * kBK * 2;
         mbar_expect_tx(&full[s], kTxBytes);
@@ -197,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = instr_desc(kBM, BN);
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % S::kStages;
-        mbar_wait(&full[s], (kb / S::kStages) & 1, err);
+        mbar_wait(&full[s], (kb / S::kStages) & 1, err, broken);
         tmem_fence_after();
         const unsigned a = smem_u32(base + s * S::kStageBytes);
         const unsigned b = a + RM * kBK * 2;
@@ -211,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // epilogue: warp w reads accumulator rows 32 (w % 4) .. + 31 (its tensor-memory lane quarter)
     const int quarter = warp & 3;
-    mbar_wait(accum, 0, err);
+    mbar_wait(accum, 0, err, broken);
     tmem_fence_after();
     const int trow = quarter * 32 + lane, row = m0 + trow;
     if (trow < RM) {
@@ -236,6 +241,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   tmem_fence_before();
+  __syncthreads();
+  if (*broken && threadIdx.x == 0) {
+    // a wait expired: before the shared memory is released, wait (bounded again) for the last
+    // loads issued into every stage
+    volatile int drain_broken = 0;
+    for (int s = 0; s < S::kStages && s < nk; ++s) {
+      const int last = s + (nk - 1 - s) / S::kStages * S::kStages;
+      mbar_wait(&full[s], (last / S::kStages) & 1, err, &drain_broken, kWaitNs / 8);
+    }
+  }
   __syncthreads();
   if (warp == 1) {
     tmem_fence_after();
