@@ -39,14 +39,11 @@ __device__ unsigned g_error;  // error word of launches that were given none
 // 128-row MMA operand A runs on into the W rows: its upper half is discarded. As many stages as
 // fit in 227 KB of shared memory: the bytes in flight set the streaming rate.
 template <int BN, int RM> struct Shape {
-  // at least the 128 rows of 128 bytes that the MMA's operand A spans
-  static constexpr int kStageBytes = (RM + BN) * kBK * 2 > kBM * kBK * 2 ? (RM + BN) * kBK * 2 : kBM * kBK * 2;
-  // 32-wide tiles leave room for two CTAs per SM
-  static constexpr int kSmemMax = BN == 32 ? 113 * 1024 : 227 * 1024;
-  static constexpr int kExtra = 1024 /* alignment */ + 512 /* barriers, flags */;
+  static constexpr int kStageBytes = (RM + BN) * kBK * 2;
+  static constexpr int kSmemMax = 227 * 1024, kExtra = 1024 /* alignment */ + 512 /* barriers, flags */;
   static constexpr int kStages = (kSmemMax - kExtra) / kStageBytes < 16 ? (kSmemMax - kExtra) / kStageBytes : 16;
   static constexpr int kSmem = kStages * kStageBytes + kExtra;
-  static_assert(kStages >= 2, "stage layout");
+  static_assert(kStages >= 2 && kBM * kBK * 2 <= kStageBytes, "stage layout");
 };
 
 __device__ __forceinline__ unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
@@ -350,9 +347,7 @@ template <int BN, int RM> cudaError_t allow_smem() {
   return cudaFuncSetAttribute(gemm_kernel<BN, RM>, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape<BN, RM>::kSmem);
 }
 cudaError_t allow_smem(int bn, int rm) {
-  if (rm == 64)
-    return bn == 256 ? allow_smem<256, 64>() : bn == 128 ? allow_smem<128, 64>() : bn == 64 ? allow_smem<64, 64>()
-                                                                                           : allow_smem<32, 64>();
+  if (rm == 64) return bn == 256 ? allow_smem<256, 64>() : bn == 128 ? allow_smem<128, 64>() : allow_smem<64, 64>();
   return bn == 256 ? allow_smem<256, kBM>() : bn == 128 ? allow_smem<128, kBM>() : allow_smem<64, kBM>();
 }
 
@@ -372,7 +367,7 @@ int rows_per_tile(int m, int n) { return m <= 64 || n < 2048 ? 64 : kBM; }
 // weighted by the bytes a tile streams per K step (time ~ waves x (rows + width); the wider on
 // ties).
 int choose_bn(int m, int n, int rm, int sms) {
-  if (n < 2048) return 32;
+  if (n < 2048) return 64;
   const int widths[3] = {256, 128, 64};
   int best = 256;
   long long best_cost = -1;
@@ -431,8 +426,7 @@ int xb::gemm_bf16(int m, int n, int k, const void *x, const void *w, void *out, 
     switch (plan.bn) {
       case 256: return launch<256, 64>(plan, m, n, k, out, ldo, err, st);
       case 128: return launch<128, 64>(plan, m, n, k, out, ldo, err, st);
-      case 64: return launch<64, 64>(plan, m, n, k, out, ldo, err, st);
-      default: return launch<32, 64>(plan, m, n, k, out, ldo, err, st);
+      default: return launch<64, 64>(plan, m, n, k, out, ldo, err, st);
     }
   }
   switch (plan.bn) {
