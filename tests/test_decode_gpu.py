@@ -253,10 +253,12 @@ def test_empty_row_keeps_state_bitwise(cuda_device):
             assert not changed[:, :5].any() and not changed[:, 6:].any(), "only slot 5 written"
 
 
-@pytest.mark.parametrize("name", ["qwen3.5-tiny", "qwen3-tiny"])
-def test_long_prefix_split_kv(name, cuda_device):
-    """One step over a 3000-slot random prefix: exercises the split-KV partials and combine."""
-    cap = 4096
+@pytest.mark.parametrize("name,L,cap", [("qwen3.5-tiny", 3000, 4096), ("qwen3-tiny", 3000, 4096),
+                                        ("qwen3.5-tiny", 12000, 12288)])
+def test_long_prefix_split_kv(name, L, cap, cuda_device):
+    """One step over a long random prefix: exercises the split-KV partials and combine. Items of
+    128 or more positions take the 32-position block loop: the Qwen3 geometry (8 KV heads, 18
+    splits) at 3000 slots, the Qwen3.5 geometry (2 KV heads, 74 splits) at 12000."""
     g, sd, W, eng = model(name, cap, cuda_device)
     full = eng.allocate_state()
     gen = torch.Generator().manual_seed(11)
@@ -266,7 +268,6 @@ def test_long_prefix_split_kv(name, cuda_device):
         t.copy_(v)
         cpu_state.append(v[:1].clone())
     state = [t.narrow(0, 0, 1) for t in full]
-    L = 3000
     ids = torch.tensor([[42]], dtype=torch.int64, device=cuda_device)
     pos = torch.tensor([[L - 1]], dtype=torch.int64, device=cuda_device)
     nxt = torch.empty(1, dtype=torch.int64, device=cuda_device)

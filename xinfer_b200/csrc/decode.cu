@@ -159,10 +159,27 @@ static size_t ubytes_for(const XbGeometry &g, int NB) {
   return (u + 127) & ~size_t(127);
 }
 
+// Which long-context kernel serves a launch of one or two rows: 0 (the standard kernel) unless a
+// split-KV item of an attention layer spans at least kAttBlockMin positions and the head geometry
+// has a long-context kernel (1: head dimension 128, G <= 2; 2: head dimension 256, G <= 4).
+static int long_attention_kind(const StepParams &p) {
+  if (p.L <= 0 || p.delta_mask == (p.L >= 64 ? ~0ull : ((1ull << p.L) - 1))) return 0;
+  int longest = 0;
+  for (int b = 0; b < p.B; ++b)
+    if (p.q_len[b] > 0) longest = std::max(longest, (p.kv_len[b] + p.splits - 1) / p.splits);
+  if (longest < kAttBlockMin) return 0;
+  const int G = p.HQ / p.HKV;
+  if (p.D == 128 && G <= 2) return 1;
+  if (p.D == 256 && G <= 4) return 2;
+  return 0;
+}
+
 template <int NB>
 static int launch(const StepParams &prm, size_t smem, int ncta, cudaStream_t stream) {
+  const int kind = NB <= 2 ? long_attention_kind(prm) : 0;
   cudaError_t e = NB >= 4 ? launch_tensor_tiles(NB, prm, smem, ncta, stream)
-                          : launch_decode<(NB >= 4 ? 1 : NB)>(prm, smem, ncta, stream);
+                  : kind ? launch_long_attention(NB, kind, prm, smem, ncta, stream)
+                         : launch_decode<(NB >= 4 ? 1 : NB)>(prm, smem, ncta, stream);
   if (e != cudaSuccess) return fail(XB_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(e));
   return XB_OK;
 }
@@ -182,6 +199,7 @@ int xb_debug_fault(int32_t withhold_stage, uint64_t wait_limit_ns) {
   if (limit < 1000000ull) return fail(XB_ERR_INVALID, "wait limit below 1 ms");
   XB_CUDA(set_fault_constants(stage, limit));
   XB_CUDA(set_fault_tensor_tiles(stage, limit));
+  XB_CUDA(set_fault_long_attention(stage, limit));
   return XB_OK;
 }
 

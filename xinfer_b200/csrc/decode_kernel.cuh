@@ -38,6 +38,7 @@
 #include <cmath>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 namespace xb {
@@ -51,6 +52,9 @@ constexpr int kHdrBytes = 512;
 constexpr int kResRows = 32;                           // residual rows a CTA owns (<= 32)
 constexpr int kResBytes = XB_MAX_BATCH * kResRows * 4;
 constexpr int kRedFloats = 1024;
+// Long-context kernels (AG > 0) run the attention items in position blocks when an item spans at
+// least this many positions (the host picks the kernel per launch).
+constexpr int kAttBlockMin = 128;
 // RoPE cos/sin of every row's position (bf16 pair per frequency), computed once per launch:
 // the positions are the same for every attention layer of the step.
 constexpr int kRopeFreqs = 64;  // rotary_dim / 2 <= 64
@@ -469,7 +473,7 @@ static __device__ __noinline__ float repoll1f(const u64 *w, unsigned tg, volatil
 // ------------------------------------------------------------------------------------------
 // Consumer role
 // ------------------------------------------------------------------------------------------
-template <int NB> struct Consumer {
+template <int NB, int AG = 0, int AE = 0> struct Consumer {
 #if XB_TENSOR_TILES
   static constexpr int kPad = 1;  // padded activation rows (tensor-core tiles)
 #else
@@ -1716,6 +1720,156 @@ template <int NB> struct Consumer {
     else delta_tiles(l);
   }
 
+  // ---- long split-KV ranges: position blocks (long-context kernels, AG > 0) -------------------
+  // Warp w takes the blocks w, w + 8, ... of PB = 32 / LPP positions of [j0, j1), with
+  // LPP = D / 128 lanes per position (each lane holds 128 elements of its position's K row). A
+  // lane issues all loads of its K elements first, then computes its partial scores for every
+  // query head of the KV head (G <= GM); it then issues the loads of its EPL elements of every V
+  // row of the block and, while they travel, updates the running maximum, the rescale and the
+  // probabilities once per block and head; P.V follows with the block's probabilities broadcast
+  // by shuffles. Rounding as the position loop (FlashAttention-2): fp32 row sums, P rounded to
+  // bf16 for P.V. The warps' partial states are merged one head at a time and written as this
+  // split's partials.
+  template <int GM, int EPL>
+  __device__ __forceinline__ void attn_blocks(const bf16 *kc, const bf16 *vc, int j0, int j1, long long pos,
+                                              int b, int kvh, int s, unsigned tg) {
+    constexpr int D = EPL * 32, LPP = EPL / 4, PB = 32 / LPP, KE = D / LPP, KQ = KE / 8;
+    const int G = p.HQ / p.HKV;
+    const float *qs = reinterpret_cast<const float *>(U);      // [G][D]
+    const float *kn = qs + G * D;                               // [D]
+    const float *vn = kn + D;                                   // [D]
+    float *mg = reinterpret_cast<float *>(U) + G * D + 2 * D;  // [kWarps][D + 2]
+    const float scale = p.att_scale;
+    const int sub = lane % LPP, pl = lane / LPP;
+    float o[GM][EPL], m[GM], ls[GM];
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      m[g] = -INFINITY;
+      ls[g] = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) o[g][e] = 0.f;
+    }
+    auto dot8 = [](const float4 &a0, const float4 &a1, const float (&k)[8], float acc) {
+      acc = fmaf(a0.x, k[0], acc); acc = fmaf(a0.y, k[1], acc); acc = fmaf(a0.z, k[2], acc);
+      acc = fmaf(a0.w, k[3], acc); acc = fmaf(a1.x, k[4], acc); acc = fmaf(a1.y, k[5], acc);
+      acc = fmaf(a1.z, k[6], acc); acc = fmaf(a1.w, k[7], acc);
+      return acc;
+    };
+    const int nblk = (j1 - j0 + PB - 1) / PB;
+    for (int blk = warp; blk < nblk; blk += kWarps) {
+      const int jb = j0 + blk * PB, j = jb + pl;
+      const bool valid = j < j1, cur = j == pos;
+      const bf16 *krow = kc + (size_t)j * D + sub * KE;
+      uint4 kr[KQ];
+#pragma unroll
+      for (int i = 0; i < KQ; ++i) kr[i] = (valid && !cur) ? ldg_u4(krow + i * 8) : make_uint4(0, 0, 0, 0);
+      float sa[GM], sb[GM];
+#pragma unroll
+      for (int g = 0; g < GM; ++g) sa[g] = sb[g] = 0.f;
+#pragma unroll
+      for (int i = 0; i < KQ; ++i) {
+        float kf[8];
+        if (cur) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) kf[e] = kn[sub * KE + i * 8 + e];
+        } else {
+          unpack8(kr[i], kf);
+        }
+#pragma unroll
+        for (int g = 0; g < GM; ++g)
+          if (g < G) {
+            const float4 *q4 = reinterpret_cast<const float4 *>(qs + g * D + sub * KE + i * 8);
+            if (i & 1) sb[g] = dot8(q4[0], q4[1], kf, sb[g]);
+            else sa[g] = dot8(q4[0], q4[1], kf, sa[g]);
+          }
+      }
+      const int cnt = min(PB, j1 - jb);
+      using VT = typename std::conditional<EPL == 8, uint4, uint2>::type;
+      VT vr[PB];
+#pragma unroll
+      for (int jj = 0; jj < PB; ++jj) {
+        const int jr = jb + jj;
+        const bool ld = jj < cnt && jr != pos;
+        if constexpr (EPL == 8) vr[jj] = ld ? ldg_u4(vc + (size_t)jr * D + lane * 8) : make_uint4(0, 0, 0, 0);
+        else vr[jj] = ld ? ldg_u2(vc + (size_t)jr * D + lane * 4) : make_uint2(0, 0);
+      }
+      // lane 0's position is always in range, so every block maximum is finite
+      float pb[GM];
+#pragma unroll
+      for (int g = 0; g < GM; ++g) {
+        pb[g] = 0.f;
+        if (g < G) {
+          float t = sa[g] + sb[g];
+          if (LPP == 2) t += __shfl_xor_sync(0xffffffffu, t, 1);
+          const float sv = valid ? t * scale : -INFINITY;
+          const float mn = fmaxf(m[g], warp_max(sv));
+          const float corr = expf(m[g] - mn);
+          const float pe = valid ? expf(sv - mn) : 0.f;
+          ls[g] = fmaf(ls[g], corr, sub == 0 ? pe : 0.f);
+          pb[g] = rbf(pe);
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) o[g][e] *= corr;
+          m[g] = mn;
+        }
+      }
+#pragma unroll
+      for (int jj = 0; jj < PB; ++jj) {
+        if (jj < cnt) {
+          float vf[8];
+          if (jb + jj == pos) {
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) vf[e] = vn[lane * EPL + e];
+          } else {
+            if constexpr (EPL == 8) unpack8(vr[jj], vf);
+            else unpack8(make_uint4(vr[jj].x, vr[jj].y, 0, 0), vf);
+          }
+#pragma unroll
+          for (int g = 0; g < GM; ++g)
+            if (g < G) {
+              const float pj = __shfl_sync(0xffffffffu, pb[g], jj * LPP);
+#pragma unroll
+              for (int e = 0; e < EPL; ++e) o[g][e] = fmaf(pj, vf[e], o[g][e]);
+            }
+        }
+      }
+    }
+    trace_mark(2);
+    const int MS = D + 2;
+    float *mw = mg + (size_t)warp * MS;
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      if (g >= G) break;
+      const float lw = warp_sum(ls[g]);
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) mw[lane * EPL + e] = o[g][e];
+      if (lane == 0) {
+        mw[D] = m[g];
+        mw[D + 1] = lw;
+      }
+      csync();
+      for (int d = tid; d < D; d += kCT) {
+        float M = -INFINITY;
+        for (int i = 0; i < kWarps; ++i) M = fmaxf(M, mg[(size_t)i * MS + D]);
+        float O = 0.f, Lw = 0.f;
+        if (M != -INFINITY) {
+          for (int i = 0; i < kWarps; ++i) {
+            const float *ms = mg + (size_t)i * MS;
+            const float mi = ms[D];
+            if (mi == -INFINITY) continue;
+            const float f = expf(mi - M);
+            O = fmaf(ms[d], f, O);
+            Lw = fmaf(ms[D + 1], f, Lw);
+          }
+        }
+        const int hq = kvh * G + g;
+        const size_t base = ((size_t)b * p.HQ + hq) * p.splits + s;
+        st_u64(p.att_o + base * D + d, ftag(O, tg));
+        if (d == 0) st_u64x2(p.att_ml + 2 * base, ftag(M, tg), ftag(Lw, tg));
+      }
+      csync();
+    }
+  }
+
   // ---- attention: q/k norm, RoPE, KV append, split-KV partials ----------------------------
   // Work item = (row b, KV head, split of the populated prefix). Warp w serves query head
   // w % G over positions j with (j - j0) / 1 % P == w / G (P = kWarps / G position lanes); the
@@ -1828,6 +1982,12 @@ template <int NB> struct Consumer {
       if (s == 0 && pos >= 0 && pos < p.C && tid < D) {
         kc[(size_t)pos * D + tid] = tobf(kn[tid]);
         vc[(size_t)pos * D + tid] = tobf(vn[tid]);
+      }
+      if constexpr (AG > 0) {
+        if (j1 - j0 >= kAttBlockMin) {
+          attn_blocks<AG, AE>(kc, vc, j0, j1, pos, b, kvh, s, tg);
+          continue;
+        }
       }
       // split-KV partial over positions [j0, j1) for query head g = warp % G
       const int g = warp % G, lane_pos = warp / G;
@@ -2038,7 +2198,7 @@ static __device__ __noinline__ void scrub_tagged(const StepParams &p) {
   __syncthreads();
 }
 
-template <int NB>
+template <int NB, int AG = 0, int AE = 0>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ StepParams p) {
   extern __shared__ __align__(1024) char smem[];
   SmemHdr *hdr = reinterpret_cast<SmemHdr *>(smem);
@@ -2095,7 +2255,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       }
     }
   } else if (!bad) {
-    Consumer<NB> c(p, hdr, red, rope, hres, U, ring);
+    Consumer<NB, AG, AE> c(p, hdr, red, rope, hres, U, ring);
     c.rope_table();
     walk_step(p, c);
     c.trace_end();
@@ -2104,15 +2264,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
 }
 
 // Host helpers of this translation unit's kernels (each compilation keeps its own constants).
-template <int NB> static cudaError_t launch_decode(const StepParams &prm, size_t smem, int ncta,
-                                                   cudaStream_t stream) {
+template <int NB, int AG = 0, int AE = 0>
+static cudaError_t launch_decode(const StepParams &prm, size_t smem, int ncta, cudaStream_t stream) {
   // The attribute is per function and process-wide; set it once to the opt-in maximum.
   static std::mutex mu;
   static bool configured = false;
   {
     std::lock_guard<std::mutex> lock(mu);
     if (!configured) {
-      const cudaError_t e = cudaFuncSetAttribute(decode_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      const cudaError_t e = cudaFuncSetAttribute(decode_kernel<NB, AG, AE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)kSmemLimit);
       if (e != cudaSuccess) return e;
       configured = true;
@@ -2120,7 +2280,7 @@ template <int NB> static cudaError_t launch_decode(const StepParams &prm, size_t
   }
   (void)smem;
   void *args[] = {const_cast<StepParams *>(&prm)};
-  return cudaLaunchCooperativeKernel((const void *)decode_kernel<NB>, dim3(ncta), dim3(kThreads), args,
+  return cudaLaunchCooperativeKernel((const void *)decode_kernel<NB, AG, AE>, dim3(ncta), dim3(kThreads), args,
                                      smem, stream);
 }
 static cudaError_t set_fault_constants(int stage, unsigned long long limit) {
@@ -2132,5 +2292,11 @@ static cudaError_t set_fault_constants(int stage, unsigned long long limit) {
 // Batch rows 4 and 8 (kernels of the tensor-core compilation, decode_tc.cu).
 cudaError_t launch_tensor_tiles(int NB, const StepParams &prm, size_t smem, int ncta, cudaStream_t stream);
 cudaError_t set_fault_tensor_tiles(int stage, unsigned long long limit);
+// One or two batch rows with long split-KV items (kernels of decode_long.cu): kind 1 for head
+// dimension 128 with up to two query heads per KV head, kind 2 for head dimension 256 with up to
+// four.
+cudaError_t launch_long_attention(int NB, int kind, const StepParams &prm, size_t smem, int ncta,
+                                  cudaStream_t stream);
+cudaError_t set_fault_long_attention(int stage, unsigned long long limit);
 
 } // namespace xb
