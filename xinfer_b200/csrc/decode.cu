@@ -177,7 +177,10 @@ static int long_attention_kind(const StepParams &p) {
 template <int NB>
 static int launch(const StepParams &prm, size_t smem, int ncta, cudaStream_t stream) {
   const int kind = NB <= 2 ? long_attention_kind(prm) : 0;
+  const bool wide = NB <= 2 && prm.H >= kWideHidden;
   cudaError_t e = NB >= 4 ? launch_tensor_tiles(NB, prm, smem, ncta, stream)
+                  : wide && kind == 2 ? launch_wide_long(NB, prm, smem, ncta, stream)
+                  : wide && kind == 0 ? launch_wide(NB, 0, prm, smem, ncta, stream)
                   : kind ? launch_long_attention(NB, kind, prm, smem, ncta, stream)
                          : launch_decode<(NB >= 4 ? 1 : NB)>(prm, smem, ncta, stream);
   if (e != cudaSuccess) return fail(XB_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(e));
@@ -200,6 +203,8 @@ int xb_debug_fault(int32_t withhold_stage, uint64_t wait_limit_ns) {
   XB_CUDA(set_fault_constants(stage, limit));
   XB_CUDA(set_fault_tensor_tiles(stage, limit));
   XB_CUDA(set_fault_long_attention(stage, limit));
+  XB_CUDA(set_fault_wide(stage, limit));
+  XB_CUDA(set_fault_wide_long(stage, limit));
   return XB_OK;
 }
 

@@ -54,7 +54,10 @@ constexpr int kResBytes = XB_MAX_BATCH * kResRows * 4;
 constexpr int kRedFloats = 1024;
 // Long-context kernels (AG > 0) run the attention items in position blocks when an item spans at
 // least this many positions (the host picks the kernel per launch).
-constexpr int kAttBlockMin = 128;
+#ifndef XB_ATT_BLOCK_MIN
+#define XB_ATT_BLOCK_MIN 128
+#endif
+constexpr int kAttBlockMin = XB_ATT_BLOCK_MIN;
 // RoPE cos/sin of every row's position (bf16 pair per frequency), computed once per launch:
 // the positions are the same for every attention layer of the step.
 constexpr int kRopeFreqs = 64;  // rotary_dim / 2 <= 64
@@ -473,7 +476,7 @@ static __device__ __noinline__ float repoll1f(const u64 *w, unsigned tg, volatil
 // ------------------------------------------------------------------------------------------
 // Consumer role
 // ------------------------------------------------------------------------------------------
-template <int NB, int AG = 0, int AE = 0> struct Consumer {
+template <int NB, int AG = 0, int AE = 0, int LK = 0> struct Consumer {
 #if XB_TENSOR_TILES
   static constexpr int kPad = 1;  // padded activation rows (tensor-core tiles)
 #else
@@ -1218,6 +1221,31 @@ template <int NB, int AG = 0, int AE = 0> struct Consumer {
     const size_t rowb = (size_t)K * 2;
     const int bsel = lane & 15;
     const bool second = lane >= 16;
+    // Kernels for wide models (LK): with few rows per ring slot and at least one tile per warp,
+    // tile t belongs to warp t % kWarps, which runs all its rows over all of K; no partial sums, no
+    // CTA barrier. Every warp still waits for and releases every slot, in order, as in the other
+    // paths.
+    if (LK && (R + 1) / 2 < kWarps && (hi - lo + R - 1) / R >= kWarps) {
+      int t = 0;
+      for (int r0 = lo; r0 < hi; r0 += R, ++t) {
+        const int n = min(R, hi - r0);
+        const char *slotp = wait_full();
+        if (slotp && t % kWarps == warp) {
+          for (int pair = 0; pair < (n + 1) / 2; ++pair) {
+            const int rA = 2 * pair, rB = min(rA + 1, n - 1);
+            const uint4 *wA = reinterpret_cast<const uint4 *>(slotp + rA * rowb);
+            const uint4 *wB = reinterpret_cast<const uint4 *>(slotp + rB * rowb);
+            const uint4 *uA = reinterpret_cast<const uint4 *>(slotp + (n + rA) * rowb);
+            const uint4 *uB = reinterpret_cast<const uint4 *>(slotp + (n + rB) * rowb);
+            const float2 r = gemv_pair<PAIRED, NB>(wA, wB, uA, uB, act4, n8, 0, n8);
+            const int row = rA + (second ? 1 : 0);
+            if (bsel < NB && bsel < p.B && row < n) epilogue(EPI, bsel, r0 + row, r.x, r.y, lo, otag);
+          }
+        }
+        release();
+      }
+      return;
+    }
     int parity = 0;
     for (int r0 = lo; r0 < hi; r0 += R, parity ^= 1) {
       const int n = min(R, hi - r0);
@@ -2198,7 +2226,7 @@ static __device__ __noinline__ void scrub_tagged(const StepParams &p) {
   __syncthreads();
 }
 
-template <int NB, int AG = 0, int AE = 0>
+template <int NB, int AG = 0, int AE = 0, int LK = 0>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ StepParams p) {
   extern __shared__ __align__(1024) char smem[];
   SmemHdr *hdr = reinterpret_cast<SmemHdr *>(smem);
@@ -2255,7 +2283,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
       }
     }
   } else if (!bad) {
-    Consumer<NB, AG, AE> c(p, hdr, red, rope, hres, U, ring);
+    Consumer<NB, AG, AE, LK> c(p, hdr, red, rope, hres, U, ring);
     c.rope_table();
     walk_step(p, c);
     c.trace_end();
@@ -2264,7 +2292,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
 }
 
 // Host helpers of this translation unit's kernels (each compilation keeps its own constants).
-template <int NB, int AG = 0, int AE = 0>
+template <int NB, int AG = 0, int AE = 0, int LK = 0>
 static cudaError_t launch_decode(const StepParams &prm, size_t smem, int ncta, cudaStream_t stream) {
   // The attribute is per function and process-wide; set it once to the opt-in maximum.
   static std::mutex mu;
@@ -2272,7 +2300,7 @@ static cudaError_t launch_decode(const StepParams &prm, size_t smem, int ncta, c
   {
     std::lock_guard<std::mutex> lock(mu);
     if (!configured) {
-      const cudaError_t e = cudaFuncSetAttribute(decode_kernel<NB, AG, AE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      const cudaError_t e = cudaFuncSetAttribute(decode_kernel<NB, AG, AE, LK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)kSmemLimit);
       if (e != cudaSuccess) return e;
       configured = true;
@@ -2280,7 +2308,7 @@ static cudaError_t launch_decode(const StepParams &prm, size_t smem, int ncta, c
   }
   (void)smem;
   void *args[] = {const_cast<StepParams *>(&prm)};
-  return cudaLaunchCooperativeKernel((const void *)decode_kernel<NB, AG, AE>, dim3(ncta), dim3(kThreads), args,
+  return cudaLaunchCooperativeKernel((const void *)decode_kernel<NB, AG, AE, LK>, dim3(ncta), dim3(kThreads), args,
                                      smem, stream);
 }
 static cudaError_t set_fault_constants(int stage, unsigned long long limit) {
@@ -2298,5 +2326,13 @@ cudaError_t set_fault_tensor_tiles(int stage, unsigned long long limit);
 cudaError_t launch_long_attention(int NB, int kind, const StepParams &prm, size_t smem, int ncta,
                                   cudaStream_t stream);
 cudaError_t set_fault_long_attention(int stage, unsigned long long limit);
+// One or two batch rows of wide models (hidden size >= kWideHidden): the kernels whose GEMV
+// stages with few rows per ring slot run one tile per warp (decode_wide.cu, and
+// decode_wide_long.cu with the long-context attention of head dimension 256).
+constexpr int kWideHidden = 2048;
+cudaError_t launch_wide(int NB, int kind, const StepParams &prm, size_t smem, int ncta, cudaStream_t stream);
+cudaError_t set_fault_wide(int stage, unsigned long long limit);
+cudaError_t launch_wide_long(int NB, const StepParams &prm, size_t smem, int ncta, cudaStream_t stream);
+cudaError_t set_fault_wide_long(int stage, unsigned long long limit);
 
 } // namespace xb
