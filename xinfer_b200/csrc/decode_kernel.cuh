@@ -1933,7 +1933,9 @@ template <int NB, int AG = 0, int AE = 0, int LK = 0> struct Consumer {
       const unsigned *x = p.proj + (size_t)b * p.pstride;
       // Long ranges: this item's K/V rows head for L2 while the query is still being computed
       // upstream (the position loop keeps too few loads in flight to pull them from HBM itself).
-      if (tid == 0 && j1 - j0 >= 64) {
+      // The long-context kernels' position blocks issue a block's loads together and do without
+      // (measured faster: the range prefetch delayed the q/k polls).
+      if (AG == 0 && tid == 0 && j1 - j0 >= 64) {
         const size_t off = (((size_t)b * HKV + kvh) * p.C + j0) * D;
         prefetch_l2(kc_all + off, (size_t)(j1 - j0) * D * 2);
         prefetch_l2(vc_all + off, (size_t)(j1 - j0) * D * 2);
