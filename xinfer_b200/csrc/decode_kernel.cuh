@@ -1749,19 +1749,20 @@ template <int NB, int AG = 0, int AE = 0, int LK = 0> struct Consumer {
   }
 
   // ---- long split-KV ranges: position blocks (long-context kernels, AG > 0) -------------------
-  // Warp w takes the blocks w, w + 8, ... of PB = 32 / LPP positions of [j0, j1), with
-  // LPP = D / 128 lanes per position (each lane holds 128 elements of its position's K row). A
-  // lane issues all loads of its K elements first, then computes its partial scores for every
-  // query head of the KV head (G <= GM); it then issues the loads of its EPL elements of every V
-  // row of the block and, while they travel, updates the running maximum, the rescale and the
-  // probabilities once per block and head; P.V follows with the block's probabilities broadcast
-  // by shuffles. Rounding as the position loop (FlashAttention-2): fp32 row sums, P rounded to
-  // bf16 for P.V. The warps' partial states are merged one head at a time and written as this
-  // split's partials.
+  // Warp w takes the blocks w, w + 8, ... of PB = 8 positions of [j0, j1), LPP = 4 lanes per
+  // position. Lane sub of a position holds the 16-byte chunks sub, sub + 4, ... of its K row, so
+  // each load instruction reads 64 contiguous bytes of every row (8 rows per instruction). A lane
+  // issues all loads of its K chunks first, computes its partial scores for every query head of
+  // the KV head (G <= GM), adds them over the position's lanes, then issues the loads of its EPL
+  // elements of every V row of the block and, while they travel, updates the running maximum,
+  // the rescale and the probabilities once per block and head; P.V follows with the block's
+  // probabilities broadcast by shuffles. Rounding as the position loop (FlashAttention-2): fp32
+  // row sums, P rounded to bf16 for P.V. The warps' partial states are merged one head at a time
+  // and written as this split's partials.
   template <int GM, int EPL>
   __device__ __forceinline__ void attn_blocks(const bf16 *kc, const bf16 *vc, int j0, int j1, long long pos,
                                               int b, int kvh, int s, unsigned tg) {
-    constexpr int D = EPL * 32, LPP = EPL / 4, PB = 32 / LPP, KE = D / LPP, KQ = KE / 8;
+    constexpr int D = EPL * 32, LPP = 4, PB = 32 / LPP, KE = D / LPP, KQ = KE / 8;
     const int G = p.HQ / p.HKV;
     const float *qs = reinterpret_cast<const float *>(U);      // [G][D]
     const float *kn = qs + G * D;                               // [D]
@@ -1787,10 +1788,10 @@ template <int NB, int AG = 0, int AE = 0, int LK = 0> struct Consumer {
     for (int blk = warp; blk < nblk; blk += kWarps) {
       const int jb = j0 + blk * PB, j = jb + pl;
       const bool valid = j < j1, cur = j == pos;
-      const bf16 *krow = kc + (size_t)j * D + sub * KE;
+      const bf16 *krow = kc + (size_t)j * D + sub * 8;
       uint4 kr[KQ];
 #pragma unroll
-      for (int i = 0; i < KQ; ++i) kr[i] = (valid && !cur) ? ldg_u4(krow + i * 8) : make_uint4(0, 0, 0, 0);
+      for (int i = 0; i < KQ; ++i) kr[i] = (valid && !cur) ? ldg_u4(krow + i * LPP * 8) : make_uint4(0, 0, 0, 0);
       float sa[GM], sb[GM];
 #pragma unroll
       for (int g = 0; g < GM; ++g) sa[g] = sb[g] = 0.f;
@@ -1799,14 +1800,14 @@ template <int NB, int AG = 0, int AE = 0, int LK = 0> struct Consumer {
         float kf[8];
         if (cur) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) kf[e] = kn[sub * KE + i * 8 + e];
+          for (int e = 0; e < 8; ++e) kf[e] = kn[(i * LPP + sub) * 8 + e];
         } else {
           unpack8(kr[i], kf);
         }
 #pragma unroll
         for (int g = 0; g < GM; ++g)
           if (g < G) {
-            const float4 *q4 = reinterpret_cast<const float4 *>(qs + g * D + sub * KE + i * 8);
+            const float4 *q4 = reinterpret_cast<const float4 *>(qs + g * D + (i * LPP + sub) * 8);
             if (i & 1) sb[g] = dot8(q4[0], q4[1], kf, sb[g]);
             else sa[g] = dot8(q4[0], q4[1], kf, sa[g]);
           }
@@ -1828,7 +1829,8 @@ template <int NB, int AG = 0, int AE = 0, int LK = 0> struct Consumer {
         pb[g] = 0.f;
         if (g < G) {
           float t = sa[g] + sb[g];
-          if (LPP == 2) t += __shfl_xor_sync(0xffffffffu, t, 1);
+#pragma unroll
+          for (int o2 = 1; o2 < LPP; o2 <<= 1) t += __shfl_xor_sync(0xffffffffu, t, o2);
           const float sv = valid ? t * scale : -INFINITY;
           const float mn = fmaxf(m[g], warp_max(sv));
           const float corr = expf(m[g] - mn);
