@@ -171,14 +171,25 @@ def test_single_row_matches_oracle(name, cuda_device):
 
 @pytest.mark.parametrize("name", ["qwen3-0.6b-l2", "qwen3.5-0.8b-l4", "qwen3.5-4b-l4"])
 def test_full_width_matches_oracle(name, cuda_device):
-    """Real hidden size, heads and 150K/248K vocabulary; shallow stack, tight bar."""
+    """Real hidden size, heads and 150K/248K vocabulary; shallow stack, tight bar.
+
+    Each step is held to the fixed full-width bar or, where the model's own rounding noise is
+    larger, to 3x the max-abs and 6x the cosine deficit by which the oracle with fp32 sums differs
+    from its fp64-sum twin at that step. At the Qwen3.5-4B width (hidden 2560) that twin spread is
+    ~0.045 max-abs / 5e-5 cosine deficit per step, and the GPU step (standard and wide-model kernels
+    alike) measured 1.5-2.5x / 2-5x of it against the oracle on different hosts; the 0.6B and 0.8B
+    widths stay under the fixed bar."""
     g, sd, W, eng = model(name, 64, cuda_device, jitter=0.1)
     sched = schedule_single(g, 6, seed=8)
     got, toks, state, _ = run_schedule_gpu(eng, g, sched, cuda_device)
     want, ostate = run_schedule_oracle(g, W, sched, 64)
+    with O.accumulate(torch.float64):
+        twin, _ = run_schedule_oracle(g, W, sched, 64)
     for s in range(len(sched)):
-        check_logits(got[s, 0], want[s, 0], f"{name} step {s}", cos_min=FULLW_COS,
-                     max_abs=FULLW_MAX_ABS)
+        d = (want[s, 0].float() - twin[s, 0].float()).abs().max().item()
+        c = 1.0 - O.cosine(want[s, 0], twin[s, 0])
+        check_logits(got[s, 0], want[s, 0], f"{name} step {s}", cos_min=min(FULLW_COS, 1.0 - 6 * c),
+                     max_abs=max(FULLW_MAX_ABS, 3 * d))
         assert int(toks[s, 0]) == int(torch.argmax(got[s, 0].float()))
     for i, (a, b) in enumerate(zip(state, ostate)):
         n = len(sched)
@@ -279,7 +290,14 @@ def test_long_prefix_split_kv(name, L, cap, cuda_device):
     logits = out[0] if isinstance(out, tuple) else out
     want, _ = O.decode_step(g, W, [42], [L - 1], cpu_state, [L], [1])
     if g.hidden >= 1024:
-        check_logits(logits[0], want[0], f"{name} L={L}", cos_min=FULLW_COS, max_abs=FULLW_MAX_ABS)
+        # full width: the fixed full-width bar, or the measured rounding noise of this step (as in
+        # test_full_width_matches_oracle) where that is larger
+        with O.accumulate(torch.float64):
+            twin, _ = O.decode_step(g, W, [42], [L - 1], cpu_state, [L], [1])
+        d = (want[0].float() - twin[0].float()).abs().max().item()
+        c = 1.0 - O.cosine(want[0], twin[0])
+        check_logits(logits[0], want[0], f"{name} L={L}", cos_min=min(FULLW_COS, 1.0 - 6 * c),
+                     max_abs=max(FULLW_MAX_ABS, 3 * d))
     else:
         check_logits(logits[0], want[0], f"{name} L={L}")
     assert int(nxt[0]) == int(torch.argmax(logits[0].float()))
