@@ -180,7 +180,7 @@ static int launch(const StepParams &prm, size_t smem, int ncta, cudaStream_t str
   const bool wide = NB <= 2 && prm.H >= kWideHidden;
   cudaError_t e = NB >= 4 ? launch_tensor_tiles(NB, prm, smem, ncta, stream)
                   : wide && kind == 2 ? launch_wide_long(NB, prm, smem, ncta, stream)
-                  : wide && kind == 0 ? launch_wide(NB, 0, prm, smem, ncta, stream)
+                  : wide && kind == 0 ? launch_wide(NB, prm, smem, ncta, stream)
                   : kind ? launch_long_attention(NB, kind, prm, smem, ncta, stream)
                          : launch_decode<(NB >= 4 ? 1 : NB)>(prm, smem, ncta, stream);
   if (e != cudaSuccess) return fail(XB_ERR_CUDA, std::string("decode launch: ") + cudaGetErrorString(e));

@@ -2334,7 +2334,7 @@ cudaError_t set_fault_long_attention(int stage, unsigned long long limit);
 // stages with few rows per ring slot run one tile per warp (decode_wide.cu, and
 // decode_wide_long.cu with the long-context attention of head dimension 256).
 constexpr int kWideHidden = 2048;
-cudaError_t launch_wide(int NB, int kind, const StepParams &prm, size_t smem, int ncta, cudaStream_t stream);
+cudaError_t launch_wide(int NB, const StepParams &prm, size_t smem, int ncta, cudaStream_t stream);
 cudaError_t set_fault_wide(int stage, unsigned long long limit);
 cudaError_t launch_wide_long(int NB, const StepParams &prm, size_t smem, int ncta, cudaStream_t stream);
 cudaError_t set_fault_wide_long(int stage, unsigned long long limit);

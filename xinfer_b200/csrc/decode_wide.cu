@@ -6,8 +6,7 @@
 
 namespace xb {
 
-cudaError_t launch_wide(int NB, int kind, const StepParams &prm, size_t smem, int ncta, cudaStream_t stream) {
-  (void)kind;
+cudaError_t launch_wide(int NB, const StepParams &prm, size_t smem, int ncta, cudaStream_t stream) {
   return NB == 1 ? launch_decode<1, 0, 0, 1>(prm, smem, ncta, stream) : launch_decode<2, 0, 0, 1>(prm, smem, ncta, stream);
 }
 
